@@ -1,0 +1,1113 @@
+// Forward-pass engine: packs a parsed KataGo net into device layouts and builds the launch plan that evaluates it
+// on boards in the padded board layout (PBL, see gemm.cuh). The plan follows the reference graph
+// (tools/bin2onnx/bin2onnx.py GraphBuilder.trunk :1477, block_stack :1271, residual/gpool/nested blocks :1243-1269,
+// transformer blocks :1359-1438, heads :1495-1531) with batch norm + activation + mask fused into the epilogue of
+// the GEMM that produces each tensor, and the residual add fused into the GEMM that closes each block.
+
+#include "engine.h"
+
+#include <cuda.h>
+
+#include <algorithm>
+#include <cmath>
+#include <cstring>
+#include <functional>
+#include <map>
+#include <mutex>
+#include <set>
+#include <tuple>
+
+#include "common.h"
+#include "kernels.cuh"
+
+namespace kc {
+
+namespace {
+
+int round_up(int a, int b) { return (a + b - 1) / b * b; }
+
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  if (!fn) {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    KC_CUDA(cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q));
+    if (!p || q != cudaDriverEntryPointSuccess) fail(KC_ERR_CUDA, "CUDA backend: cuTensorMapEncodeTiled unavailable");
+    fn = reinterpret_cast<EncodeTiledFn>(p);
+  }
+  return fn;
+}
+
+// 2D tensor map over a row-major [rows][cols] matrix of 2-byte elements, box [box_rows][64 elements], 128B swizzle.
+CUtensorMap make_map(const void* base, bool bf16, int cols, int rows, int box_rows) {
+  CUtensorMap map;
+  cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)cols * 2};
+  cuuint32_t box[2] = {64, (cuuint32_t)box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  if ((reinterpret_cast<uintptr_t>(base) & 15) != 0 || (cols * 2) % 16 != 0 || cols % 64 != 0)
+    fail(KC_ERR_INVALID, "CUDA backend: tensor map operand not 16-byte aligned");
+  CUresult r = encode_fn()(&map, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2,
+                           const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                           CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                           CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) fail(KC_ERR_CUDA, "CUDA backend: cuTensorMapEncodeTiled failed (" + std::to_string((int)r) + ")");
+  return map;
+}
+
+// Opt the kernel instances into large dynamic shared memory, once per device (plan-build time, never while a
+// stream is being captured).
+template <typename K>
+void allow_smem(K* kernel, int bytes) {
+  static std::mutex mu;
+  static std::set<std::pair<const void*, int>> done;
+  int dev = 0;
+  KC_CUDA(cudaGetDevice(&dev));
+  std::lock_guard<std::mutex> lock(mu);
+  auto key = std::make_pair(reinterpret_cast<const void*>(kernel), dev);
+  if (done.count(key)) return;
+  KC_CUDA(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes));
+  done.insert(key);
+}
+
+template <typename T, int BN>
+void launch_tc_bn(bool prepare, int grid, cudaStream_t s, const CUtensorMap& a, const CUtensorMap& b,
+                  const GemmParams& p) {
+  using C = TcCfg<BN>;
+  if (prepare) {
+    allow_smem(gemm_tc_kernel<T, BN>, C::SMEM);
+    return;
+  }
+  gemm_tc_kernel<T, BN><<<grid, C::THREADS, C::SMEM, s>>>(a, b, p);
+}
+
+template <typename T>
+void launch_tc(bool prepare, int bn, int grid, cudaStream_t s, const CUtensorMap& a, const CUtensorMap& b,
+               const GemmParams& p) {
+  switch (bn) {
+    case 16: launch_tc_bn<T, 16>(prepare, grid, s, a, b, p); break;
+    case 32: launch_tc_bn<T, 32>(prepare, grid, s, a, b, p); break;
+    case 48: launch_tc_bn<T, 48>(prepare, grid, s, a, b, p); break;
+    case 64: launch_tc_bn<T, 64>(prepare, grid, s, a, b, p); break;
+    case 96: launch_tc_bn<T, 96>(prepare, grid, s, a, b, p); break;
+    case 128: launch_tc_bn<T, 128>(prepare, grid, s, a, b, p); break;
+    case 192: launch_tc_bn<T, 192>(prepare, grid, s, a, b, p); break;
+    case 256: launch_tc_bn<T, 256>(prepare, grid, s, a, b, p); break;
+    default: fail(KC_ERR_INVALID, "CUDA backend: unsupported GEMM tile width " + std::to_string(bn));
+  }
+}
+
+// RoPE tables [tables][361][half] (desc.cpp computeRopeCosSin as restated in bin2onnx.py:449-484: float32 steps,
+// cos/sin of the float32 angle evaluated in float64 and rounded).
+void rope_tables(const BlockDesc& b, std::vector<float>& cs, std::vector<float>& sn, int& tables) {
+  const int half = b.head_dim / 2, P = half;
+  if (b.learnable_rope) {
+    tables = b.kv_heads;
+    cs.assign((size_t)tables * 361 * half, 0.0f);
+    sn.assign(cs.size(), 0.0f);
+    for (int h = 0; h < b.kv_heads; h++)
+      for (int p = 0; p < P; p++) {
+        float fx = b.rope_freqs[((size_t)h * P + p) * 2], fy = b.rope_freqs[((size_t)h * P + p) * 2 + 1];
+        for (int s = 0; s < 361; s++) {
+          volatile float ax = (float)(s % 19) * fx;
+          volatile float ay = (float)(s / 19) * fy;
+          volatile float a = (float)ax + (float)ay;
+          cs[((size_t)h * 361 + s) * half + p] = (float)std::cos((double)a);
+          sn[((size_t)h * 361 + s) * half + p] = (float)std::sin((double)a);
+        }
+      }
+  } else {
+    tables = 1;
+    cs.assign((size_t)361 * half, 0.0f);
+    sn.assign(cs.size(), 0.0f);
+    int ppd = P / 2, dim_half = b.head_dim / 2;
+    for (int p = 0; p < P; p++) {
+      int padj = p < ppd ? p : p - ppd;
+      volatile float expo = (float)(2 * padj) / (float)dim_half;
+      float powv = (float)std::pow((double)b.rope_theta, (double)(float)expo);
+      volatile float freq = 1.0f / powv;
+      for (int s = 0; s < 361; s++) {
+        float pos = p < ppd ? (float)(s / 19) : (float)(s % 19);
+        volatile float a = pos * (float)freq;
+        cs[(size_t)s * half + p] = (float)std::cos((double)a);
+        sn[(size_t)s * half + p] = (float)std::sin((double)a);
+      }
+    }
+  }
+}
+
+struct BnAct {
+  const BNDesc* bn = nullptr;
+  Act act = ACT_IDENTITY;
+};
+
+bool is_conv_block(const BlockDesc& b) {
+  return b.kind == BLOCK_ORDINARY || b.kind == BLOCK_GPOOL || b.kind == BLOCK_NESTED;
+}
+
+// The batch norm that the consumer of a block stack's stream applies first: the next block's pre-BN, or `after`.
+BnAct consumer_bn(const std::vector<BlockDesc>& v, size_t i, BnAct after) {
+  if (i < v.size()) {
+    if (is_conv_block(v[i])) return {&v[i].pre_bn, v[i].pre_act};
+    return {};
+  }
+  return after;
+}
+
+struct Tensor {
+  void* p = nullptr;
+  int ld = 0;
+  bool f32 = false;  // float32 storage (the residual stream of the bf16 tier) instead of the tier's type
+};
+
+}  // namespace
+
+struct Engine::Impl {
+  std::vector<void*> allocs;
+  int sm_count = 148;
+  int R = 0;
+  int stem_rows = 0;
+  const float* in_spatial = nullptr;
+  const float* in_global = nullptr;
+  const float* in_meta = nullptr;
+  float* out = nullptr;
+  int* d_err = nullptr;
+  float* rowmask = nullptr;
+  float* mask_sum = nullptr;
+  float* scale1 = nullptr;
+  float* scale2 = nullptr;
+  float* board_bias = nullptr;
+  std::map<std::tuple<int, const void*, const void*, const void*, void*>, cudaGraphExec_t> graphs;
+
+  void* alloc(size_t bytes) {
+    void* p = nullptr;
+    KC_CUDA(cudaMalloc(&p, bytes));
+    allocs.push_back(p);
+    KC_CUDA(cudaMemset(p, 0, bytes));
+    return p;
+  }
+  template <typename U>
+  U* upload(const std::vector<U>& v) {
+    if (v.empty()) return nullptr;
+    U* p = static_cast<U*>(alloc(v.size() * sizeof(U)));
+    KC_CUDA(cudaMemcpy(p, v.data(), v.size() * sizeof(U), cudaMemcpyHostToDevice));
+    return p;
+  }
+  ~Impl() {
+    for (auto& g : graphs) cudaGraphExecDestroy(g.second);
+    for (void* p : allocs) cudaFree(p);
+  }
+};
+
+// ================================================================================================================
+// Plan builder. Runs twice: pass 0 sizes the shared scratch tensors, pass 1 allocates and records launches.
+// ================================================================================================================
+
+namespace {
+
+enum Role : int {
+  R_T1, R_REG, R_G, R_XN, R_QKV, R_O, R_H, R_AG, R_HEAD, R_P1A, R_STEM,
+  R_LEVEL0 = 16,  // + 2 * depth (+0 stream, +1 act)
+  R_COUNT = 32
+};
+enum FRole : int { F_POOL, F_GBIAS, F_VPOOL, F_V2, F_PASS, F_COUNT };
+
+template <typename T>
+struct Builder {
+  Engine::Impl& I;
+  std::vector<Engine::Launch>& plan;
+  const ModelDesc& m;
+  int max_batch;
+  int pass = 0;
+  bool tc;
+  bool bf16;
+  int ld_max[R_COUNT] = {0};
+  int rows_of[R_COUNT] = {0};
+  Tensor tens[R_COUNT];
+  int f_max[F_COUNT] = {0};
+  float* fbuf[F_COUNT] = {nullptr};
+  int stem_k = 1, stem_pad = 0, stem_stride = 20, stem_brows = 400, stem_cin = 64;
+
+  Builder(Engine::Impl& i, std::vector<Engine::Launch>& pl, const ModelDesc& md, int mb, bool bf)
+      : I(i), plan(pl), m(md), max_batch(mb), tc(sizeof(T) == 2), bf16(bf) {}
+
+  int pbl_rows_alloc() const { return round_up(max_batch * 400, 128) + 128; }
+
+  // The residual streams (trunk and nested-block levels) are float32 in the bf16 tier: bf16's 8-bit mantissa
+  // would otherwise round every residual add.
+  bool is_stream(int role) const { return role >= R_LEVEL0 && (role - R_LEVEL0) % 2 == 0; }
+
+  Tensor tensor(int role, int c) {
+    int ld = round_up(std::max(c, 16), 64);
+    if (pass == 0) {
+      ld_max[role] = std::max(ld_max[role], ld);
+      return {};
+    }
+    if (ld > tens[role].ld) fail(KC_ERR_INVALID, "CUDA backend: internal scratch sizing error");
+    return tens[role];
+  }
+  float* fbuffer(int role, int per_board) {
+    if (pass == 0) {
+      f_max[role] = std::max(f_max[role], per_board);
+      return nullptr;
+    }
+    return fbuf[role];
+  }
+  void allocate() {
+    for (int r = 0; r < R_COUNT; r++) {
+      if (!ld_max[r]) continue;
+      int rows = r == R_STEM ? I.stem_rows : I.R;
+      tens[r].ld = ld_max[r];
+      tens[r].f32 = bf16 && is_stream(r);
+      tens[r].p = I.alloc((size_t)rows * ld_max[r] * (tens[r].f32 ? sizeof(float) : sizeof(T)));
+      rows_of[r] = rows;
+    }
+    for (int f = 0; f < F_COUNT; f++)
+      if (f_max[f]) fbuf[f] = static_cast<float*>(I.alloc((size_t)max_batch * f_max[f] * sizeof(float)));
+  }
+  int rows_for(const Tensor& t) const {
+    for (int r = 0; r < R_COUNT; r++)
+      if (tens[r].p == t.p) return rows_of[r];
+    return I.R;
+  }
+
+  template <typename U>
+  U* up(const std::vector<U>& v) { return pass == 0 ? nullptr : I.upload(v); }
+
+  void add(int cls, std::function<void(cudaStream_t, int)> fn) {
+    if (pass == 1) plan.push_back({cls, std::move(fn)});
+  }
+
+  // ---- weights ----
+  // W [N][taps * cin_pad]: conv (file order [ky][kx][ic][oc]) at output rows [n_off, n_off + oc)
+  static void pack_conv(std::vector<float>& W, int K, int cin_pad, int n_off, const ConvDesc& c) {
+    for (int ky = 0; ky < c.ky; ky++)
+      for (int kx = 0; kx < c.kx; kx++)
+        for (int i = 0; i < c.ic; i++)
+          for (int o = 0; o < c.oc; o++)
+            W[(size_t)(n_off + o) * K + (ky * c.kx + kx) * cin_pad + i] =
+                c.w[(((size_t)ky * c.kx + kx) * c.ic + i) * c.oc + o];
+  }
+  static void pack_linear(std::vector<float>& W, int K, int n_off, const MatMulDesc& mm, const int* perm = nullptr,
+                          int ncols = -1, int col0 = 0) {
+    if (ncols < 0) ncols = mm.oc;
+    for (int o = 0; o < ncols; o++)
+      for (int i = 0; i < mm.ic; i++)
+        W[(size_t)(n_off + o) * K + i] = mm.w[(size_t)i * mm.oc + (perm ? perm[col0 + o] : col0 + o)];
+  }
+
+  // ---- GEMM ----
+  struct Seg {
+    int width = 0;
+    int flags = 0;
+    int act = 0;
+    std::vector<float> scale, bias;
+    const float* board_bias = nullptr;
+    int ld_bb = 0;
+    Tensor res, raw, actout;
+    int res_c0 = 0, raw_c0 = 0, act_c0 = 0;
+  };
+
+  struct Spec {
+    int cls = CLS_LINEAR;
+    Tensor A;
+    int cin = 0;
+    std::vector<int> taps{0};
+    int N = 0;
+    std::vector<float> W;
+    int mode = MODE_SEGMENTS;
+    std::vector<Seg> segs;
+    bool stem = false;
+    // RoPE (MODE_ROPE)
+    const float* rope_cos = nullptr;
+    const float* rope_sin = nullptr;
+    int rope_table_stride = 0, rope_q_cols = 0, rope_rot_cols = 0, head_dim = 0, rope_group = 1;
+  };
+
+  static int pick_bn(int N, int mult) {
+    const int cands[] = {256, 192, 128, 96, 64, 48, 32, 16};
+    for (int c : cands)
+      if (N % c == 0 && c % mult == 0) return c;
+    return 0;
+  }
+
+  void gemm(Spec s) {
+    if (pass == 0) return;
+    GemmParams p;
+    p.n_total = s.N;
+    p.cin = s.cin;
+    p.taps = (int)s.taps.size();
+    for (int i = 0; i < p.taps; i++) p.tap_off[i] = s.taps[i];
+    p.mode = s.mode;
+    p.nseg = (int)s.segs.size();
+    int n0 = 0;
+    for (int i = 0; i < p.nseg; i++) {
+      Seg& g = s.segs[i];
+      EpiSeg& e = p.seg[i];
+      e.n0 = n0;
+      e.n1 = n0 + g.width;
+      n0 = e.n1;
+      e.flags = g.flags;
+      e.act = g.act;
+      if (g.flags & EPI_ACT) {
+        g.scale.resize(g.width, 0.0f);
+        g.bias.resize(g.width, 0.0f);
+        e.scale = up(g.scale);
+        e.bias = up(g.bias);
+      }
+      e.board_bias = g.board_bias;
+      e.ld_bb = g.ld_bb;
+      e.res = g.res.p;
+      e.ld_res = g.res.ld;
+      e.res_c0 = g.res_c0;
+      e.out_raw = g.raw.p;
+      e.ld_raw = g.raw.ld;
+      e.raw_c0 = g.raw_c0;
+      e.out_act = g.actout.p;
+      e.ld_act = g.actout.ld;
+      e.act_c0 = g.act_c0;
+    }
+    if (s.mode == MODE_SEGMENTS && n0 != s.N) fail(KC_ERR_INVALID, "CUDA backend: GEMM segment widths != N");
+    p.rope_cos = s.rope_cos;
+    p.rope_sin = s.rope_sin;
+    p.rope_table_stride = s.rope_table_stride;
+    p.rope_q_cols = s.rope_q_cols;
+    p.rope_rot_cols = s.rope_rot_cols;
+    p.head_dim = s.head_dim;
+    p.rope_group = s.rope_group;
+    p.err = I.d_err;
+    if (s.stem) {
+      p.g.board_rows = stem_brows;
+      p.g.stride = stem_stride;
+      p.g.pad = stem_pad;
+      p.g.remap = 1;
+    }
+    p.g.rowmask = I.rowmask;
+    const int brows = p.g.board_rows;
+    const int a_rows = rows_for(s.A);
+    if (s.cin > s.A.ld) fail(KC_ERR_INVALID, "CUDA backend: GEMM reads more channels than its input holds");
+    const int K = p.taps * s.cin;
+    Engine::Impl* Ip = &I;
+    if constexpr (sizeof(T) == 2) {
+      int bn = pick_bn(s.N, s.mode == MODE_SWIGLU ? 32 : s.mode == MODE_ROPE ? s.head_dim : 16);
+      if (!bn) fail(KC_ERR_INVALID, "CUDA backend: no GEMM tile width for N = " + std::to_string(s.N));
+      std::vector<float> Wp = s.W;
+      if (s.mode == MODE_SWIGLU) {
+        // columns [0, F) = linear1, [F, 2F) = gate  ->  per tile of bn: [bn/2 linear1 | bn/2 gate]
+        const int F = s.N / 2, hb = bn / 2;
+        for (int t = 0; t < s.N / bn; t++)
+          for (int j = 0; j < hb; j++) {
+            std::memcpy(&Wp[(size_t)(t * bn + j) * K], &s.W[(size_t)(t * hb + j) * K], K * sizeof(float));
+            std::memcpy(&Wp[(size_t)(t * bn + hb + j) * K], &s.W[(size_t)(F + t * hb + j) * K], K * sizeof(float));
+          }
+      }
+      std::vector<T> Wt(Wp.size());
+      for (size_t i = 0; i < Wp.size(); i++) Wt[i] = T(Wp[i]);
+      T* dW = up(Wt);
+      CUtensorMap ta = make_map(s.A.p, bf16, s.A.ld, a_rows, 128);
+      CUtensorMap tb = make_map(dW, bf16, K, s.N, bn);
+      if (s.cin % 64 != 0) fail(KC_ERR_INVALID, "CUDA backend: GEMM input channels not padded");
+      launch_tc<T>(true, bn, 0, 0, ta, tb, p);
+      add(s.cls, [=](cudaStream_t st, int n) {
+        GemmParams q = p;
+        q.g.rows = n * brows;
+        int tiles = ((q.g.rows + 127) / 128) * (q.n_total / bn);
+        int grid = std::min(tiles, Ip->sm_count);
+        launch_tc<T>(false, bn, grid, st, ta, tb, q);
+      });
+    } else {
+      p.a = s.A.p;
+      p.lda = s.A.ld;
+      p.a_rows = a_rows;
+      p.w = up(s.W);
+      if (s.mode != MODE_SEGMENTS) fail(KC_ERR_INVALID, "CUDA backend: fused SwiGLU/RoPE needs the tensor-core path");
+      add(s.cls, [=](cudaStream_t st, int n) {
+        GemmParams q = p;
+        q.g.rows = n * brows;
+        dim3 grid((q.g.rows + 63) / 64, (q.n_total + 63) / 64);
+        gemm_simt_kernel<T><<<grid, 256, 0, st>>>(q);
+      });
+    }
+  }
+
+  std::vector<int> taps_pbl(int k) {
+    std::vector<int> t;
+    for (int ky = 0; ky < k; ky++)
+      for (int kx = 0; kx < k; kx++) t.push_back((ky - k / 2) * 20 + (kx - k / 2));
+    return t;
+  }
+
+  void check_conv(const ConvDesc& c) {
+    if (!((c.ky == 1 && c.kx == 1) || (c.ky == 3 && c.kx == 3)) || c.dy != 1 || c.dx != 1)
+      fail(KC_ERR_INVALID, "CUDA backend: " + c.name + ": only 1x1 and 3x3 undilated convolutions are supported "
+                           "inside the trunk and heads");
+  }
+
+  // conv from A (channels cin) into segments; returns the Spec with W packed
+  Spec conv_spec(int cls, Tensor A, int cin, const std::vector<const ConvDesc*>& convs, std::vector<Seg> segs) {
+    Spec s;
+    s.cls = cls;
+    s.A = A;
+    s.cin = round_up(cin, tc ? 64 : 16);
+    int k = convs[0]->ky;
+    for (auto* c : convs) {
+      check_conv(*c);
+      if (c->ky != k) fail(KC_ERR_INVALID, "CUDA backend: fused convolutions differ in size");
+    }
+    s.taps = taps_pbl(k);
+    s.N = 0;
+    for (auto& g : segs) s.N += g.width;
+    const int K = (int)s.taps.size() * s.cin;
+    if (pass == 1) {
+      s.W.assign((size_t)s.N * K, 0.0f);
+      int off = 0;
+      for (size_t i = 0; i < convs.size(); i++) {
+        pack_conv(s.W, K, s.cin, off, *convs[i]);
+        off += segs[i].width;
+      }
+    }
+    s.segs = std::move(segs);
+    return s;
+  }
+
+  static int w16(int c) { return round_up(c, 16); }
+
+  Seg act_seg(int width, const BNDesc& bn, Act act, Tensor out, int c0 = 0) {
+    Seg g;
+    g.width = width;
+    g.flags = EPI_ACT;
+    g.act = act;
+    g.scale = bn.merged_scale;
+    g.bias = bn.merged_bias;
+    g.actout = out;
+    g.act_c0 = c0;
+    return g;
+  }
+  // residual-closing segment: y = acc (* mask) + X; X = y; XA = act(next(y))
+  Seg close_seg(int width, Tensor X, Tensor XA, BnAct next, bool mask_acc) {
+    Seg g;
+    g.width = width;
+    g.flags = EPI_RESIDUAL | EPI_RAW | (mask_acc ? EPI_MASK_ACC : 0) | (X.f32 ? EPI_RES_F32 | EPI_RAW_F32 : 0);
+    g.res = X;
+    g.raw = X;
+    if (next.bn) {
+      g.flags |= EPI_ACT;
+      g.act = next.act;
+      g.scale = next.bn->merged_scale;
+      g.bias = next.bn->merged_bias;
+      g.actout = XA;
+    }
+    return g;
+  }
+
+  // ---- elementwise / reduction launches ----
+  void bias_bnact(Tensor x, int xc0, const float* board_bias, const BNDesc& bn, Act act, int C, Tensor y) {
+    const float* sc = up(bn.merged_scale);
+    const float* bi = up(bn.merged_bias);
+    Engine::Impl* Ip = &I;
+    const int Cw = y.ld;
+    add(CLS_OTHER, [=](cudaStream_t st, int n) {
+      int rows = n * 400;
+      size_t total = (size_t)rows * Cw;
+      bias_bnact_kernel<T><<<(unsigned)((total + 255) / 256), 256, 0, st>>>(
+          (const T*)x.p, x.ld, xc0, board_bias, sc, bi, act, Ip->rowmask, rows, C, Cw, (T*)y.p, y.ld);
+    });
+  }
+  void pool(Tensor x, int c0, int C, bool value_mode, float* out) {
+    Engine::Impl* Ip = &I;
+    add(CLS_OTHER, [=](cudaStream_t st, int n) {
+      dim3 grid(n, (C + 31) / 32);
+      pool_kernel<T><<<grid, dim3(32, 8), 0, st>>>((const T*)x.p, x.ld, c0, C, Ip->rowmask, Ip->mask_sum, Ip->scale1,
+                                                   Ip->scale2, value_mode ? 1 : 0, out);
+    });
+  }
+  void fc(const float* in, int in_ld, const MatMulDesc& mm, const MatBiasDesc* mb, Act act, float* out, int out_ld,
+          int out_off, int out_stride) {
+    const float* w = up(mm.w);
+    const float* b = mb ? up(mb->b) : nullptr;
+    int ic = mm.ic, oc = mm.oc;
+    float** outp = nullptr;
+    (void)outp;
+    Engine::Impl* Ip = &I;
+    const bool to_out = out == nullptr;  // null = the forward's output rows
+    add(CLS_OTHER, [=](cudaStream_t st, int n) {
+      float* o = to_out ? Ip->out : out;
+      fc_kernel<<<n, 128, ic * sizeof(float), st>>>(in, in_ld, ic, w, oc, b, act, o, out_ld, out_off, out_stride);
+    });
+  }
+  void rmsnorm(Tensor x, int C, const TfRmsDesc& d, Tensor y) {
+    const float* w = up(d.w);
+    float eps = d.eps;
+    Engine::Impl* Ip = &I;
+    add(CLS_OTHER, [=](cudaStream_t st, int n) {
+      int rows = n * 400;
+      if (x.f32)
+        rmsnorm_kernel<float, T><<<(rows + 7) / 8, 256, 0, st>>>((const float*)x.p, x.ld, C, w, eps, Ip->rowmask, rows,
+                                                                (T*)y.p, y.ld);
+      else
+        rmsnorm_kernel<T, T><<<(rows + 7) / 8, 256, 0, st>>>((const T*)x.p, x.ld, C, w, eps, Ip->rowmask, rows,
+                                                            (T*)y.p, y.ld);
+    });
+  }
+
+  // ---- blocks ----
+  void emit_stack(const std::vector<BlockDesc>& v, int depth, int C, BnAct after) {
+    for (size_t i = 0; i < v.size(); i++) emit_block(v[i], depth, C, consumer_bn(v, i + 1, after));
+  }
+
+  void emit_block(const BlockDesc& b, int depth, int C, BnAct next) {
+    Tensor X = tensor(R_LEVEL0 + 2 * depth, C);
+    Tensor XA = tensor(R_LEVEL0 + 2 * depth + 1, C);
+    if (b.kind == BLOCK_ORDINARY) {
+      // bin2onnx.py residual_block :1243-1248
+      Tensor T1 = tensor(R_T1, b.regular.oc);
+      gemm(conv_spec(CLS_CONV3, XA, C, {&b.regular}, {act_seg(w16(b.regular.oc), b.mid_bn, b.mid_act, T1)}));
+      gemm(conv_spec(b.final_conv.ky == 3 ? CLS_CONV3 : CLS_LINEAR, T1, b.final_conv.ic, {&b.final_conv},
+                     {close_seg(w16(C), X, XA, next, false)}));
+    } else if (b.kind == BLOCK_GPOOL) {
+      // bin2onnx.py gpool_block :1250-1261: regular and gpool convs share one GEMM
+      const int rc = b.regular.oc, gc = b.gpool_conv.oc;
+      Tensor REG = tensor(R_REG, rc), G = tensor(R_G, gc), T1 = tensor(R_T1, rc);
+      Seg s0;
+      s0.width = w16(rc);
+      s0.flags = EPI_RAW;
+      s0.raw = REG;
+      gemm(conv_spec(CLS_CONV3, XA, C, {&b.regular, &b.gpool_conv},
+                     {s0, act_seg(w16(gc), b.gpool_bn, b.gpool_act, G)}));
+      float* pooled = fbuffer(F_POOL, 3 * gc);
+      float* gbias = fbuffer(F_GBIAS, rc);
+      pool(G, 0, gc, false, pooled);
+      fc(pooled, 3 * gc, b.gpool_to_bias, nullptr, ACT_IDENTITY, gbias, rc, 0, 1);
+      bias_bnact(REG, 0, gbias, b.mid_bn, b.mid_act, rc, T1);
+      gemm(conv_spec(CLS_CONV3, T1, rc, {&b.final_conv}, {close_seg(w16(C), X, XA, next, false)}));
+    } else if (b.kind == BLOCK_NESTED) {
+      // bin2onnx.py nested_bottleneck_block :1263-1269
+      const int mid = b.pre_conv.oc;
+      Tensor M = tensor(R_LEVEL0 + 2 * (depth + 1), mid);
+      Tensor MA = tensor(R_LEVEL0 + 2 * (depth + 1) + 1, mid);
+      BnAct first = consumer_bn(b.inner, 0, {&b.post_bn, b.post_act});
+      Seg s;
+      s.width = w16(mid);
+      s.flags = EPI_RAW | (M.f32 ? EPI_RAW_F32 : 0);
+      s.raw = M;
+      if (first.bn) {
+        s.flags |= EPI_ACT;
+        s.act = first.act;
+        s.scale = first.bn->merged_scale;
+        s.bias = first.bn->merged_bias;
+        s.actout = MA;
+      }
+      gemm(conv_spec(CLS_LINEAR, XA, C, {&b.pre_conv}, {s}));
+      emit_stack(b.inner, depth + 1, mid, {&b.post_bn, b.post_act});
+      gemm(conv_spec(CLS_LINEAR, MA, mid, {&b.post_conv}, {close_seg(w16(C), X, XA, next, false)}));
+    } else if (b.kind == BLOCK_ATTENTION) {
+      emit_attention(b, X, XA, C, next);
+    } else {
+      emit_ffn(b, X, XA, C, next);
+    }
+  }
+
+  void emit_attention(const BlockDesc& b, Tensor X, Tensor XA, int C, BnAct next) {
+    // bin2onnx.py transformer_attention_block :1359-1423
+    const int nh = b.heads, nkv = b.kv_heads, hd = b.head_dim, vhd = b.v_head_dim;
+    if (vhd != hd) fail(KC_ERR_INVALID, "CUDA backend: " + b.name + ": vHeadDim != qHeadDim is not supported");
+    if (hd != 16 && hd != 32 && hd != 64)
+      fail(KC_ERR_INVALID, "CUDA backend: " + b.name + ": head dim must be 16, 32 or 64");
+    const int qc = nh * hd, kc = nkv * hd, vc = nkv * vhd, N = qc + kc + vc;
+    Tensor XN = tensor(R_XN, C), QKV = tensor(R_QKV, N), O = tensor(R_O, nh * vhd);
+    rmsnorm(X, C, b.ln, XN);
+    // Q and K columns permuted per head to [x0 of each pair..., x1 of each pair...] (bin2onnx.py :1369-1374)
+    std::vector<int> pq, pk;
+    for (int h = 0; h < nh; h++) {
+      for (int j = 0; j < hd; j += 2) pq.push_back(h * hd + j);
+      for (int j = 1; j < hd; j += 2) pq.push_back(h * hd + j);
+    }
+    for (int h = 0; h < nkv; h++) {
+      for (int j = 0; j < hd; j += 2) pk.push_back(h * hd + j);
+      for (int j = 1; j < hd; j += 2) pk.push_back(h * hd + j);
+    }
+    Spec s;
+    s.cls = CLS_LINEAR;
+    s.A = XN;
+    s.cin = round_up(C, tc ? 64 : 16);
+    s.N = N;
+    if (pass == 1) {
+      const int K = s.cin;
+      s.W.assign((size_t)N * K, 0.0f);
+      pack_linear(s.W, K, 0, b.q, b.use_rope ? pq.data() : nullptr);
+      pack_linear(s.W, K, qc, b.k, b.use_rope ? pk.data() : nullptr);
+      pack_linear(s.W, K, qc + kc, b.v);
+    }
+    const float* dcos = nullptr;
+    const float* dsin = nullptr;
+    int tables = 1;
+    if (b.use_rope) {
+      std::vector<float> cs, sn;
+      rope_tables(b, cs, sn, tables);
+      dcos = up(cs);
+      dsin = up(sn);
+    }
+    const int tstride = b.use_rope && b.learnable_rope ? 361 * (hd / 2) : 0;
+    const bool fuse_rope = tc && b.use_rope && hd % 32 == 0;
+    if (fuse_rope) {
+      s.mode = MODE_ROPE;
+      Seg g;
+      g.width = N;
+      g.raw = QKV;
+      s.segs = {g};
+      s.rope_cos = dcos;
+      s.rope_sin = dsin;
+      s.rope_table_stride = tstride;
+      s.rope_q_cols = qc;
+      s.rope_rot_cols = qc + kc;
+      s.head_dim = hd;
+      s.rope_group = nh / nkv;
+    } else {
+      Seg g;
+      g.width = N;
+      g.flags = EPI_RAW;
+      g.raw = QKV;
+      s.segs = {g};
+    }
+    gemm(std::move(s));
+    Engine::Impl* Ip = &I;
+    if (b.use_rope && !fuse_rope) {
+      const int group = nh / nkv;
+      add(CLS_OTHER, [=](cudaStream_t st, int n) {
+        int rows = n * 400;
+        size_t total = (size_t)rows * ((qc + kc) / 2);
+        rope_kernel<T><<<(unsigned)((total + 255) / 256), 256, 0, st>>>((T*)QKV.p, QKV.ld, qc, kc, hd, dcos, dsin,
+                                                                        tstride, group, rows);
+      });
+    }
+    // attention
+    const float scale = 1.0f / std::sqrt((float)hd);
+    if (pass == 1) {
+      const int smem_need = 361 * hd * (int)sizeof(T) * 2 + 361 * (int)sizeof(float);
+      if (hd == 16) allow_smem(attention_simt_kernel<T, 16>, smem_need);
+      else if (hd == 32) allow_smem(attention_simt_kernel<T, 32>, smem_need);
+      else allow_smem(attention_simt_kernel<T, 64>, smem_need);
+    }
+    add(CLS_ATTN, [=](cudaStream_t st, int n) {
+      dim3 grid(4, nh, n);
+      size_t smem = (size_t)361 * hd * sizeof(T) * 2 + 361 * sizeof(float);
+      switch (hd) {
+        case 16: launch_attn<16>(grid, smem, st, QKV, qc, kc, nh, nkv, scale, Ip->rowmask, O); break;
+        case 32: launch_attn<32>(grid, smem, st, QKV, qc, kc, nh, nkv, scale, Ip->rowmask, O); break;
+        default: launch_attn<64>(grid, smem, st, QKV, qc, kc, nh, nkv, scale, Ip->rowmask, O); break;
+      }
+    });
+    // output projection, masked, + residual (bin2onnx.py :1420-1423)
+    Spec so;
+    so.cls = CLS_LINEAR;
+    so.A = O;
+    so.cin = round_up(nh * vhd, tc ? 64 : 16);
+    so.N = w16(C);
+    if (pass == 1) {
+      so.W.assign((size_t)so.N * so.cin, 0.0f);
+      pack_linear(so.W, so.cin, 0, b.out);
+    }
+    so.segs = {close_seg(w16(C), X, XA, next, true)};
+    gemm(std::move(so));
+  }
+
+  template <int HD>
+  static void launch_attn(dim3 grid, size_t smem, cudaStream_t st, Tensor QKV, int qc, int kc, int nh, int nkv,
+                          float scale, const float* rowmask, Tensor O) {
+    attention_simt_kernel<T, HD><<<grid, 128, smem, st>>>((const T*)QKV.p, QKV.ld, qc, kc, nh, nkv, scale, rowmask,
+                                                         (T*)O.p, O.ld);
+  }
+
+  void emit_ffn(const BlockDesc& b, Tensor X, Tensor XA, int C, BnAct next) {
+    // bin2onnx.py transformer_ffn_block :1425-1438 (SwiGLU)
+    const int F = b.ffn;
+    Tensor XN = tensor(R_XN, C), H = tensor(R_H, F);
+    rmsnorm(X, C, b.ln, XN);
+    Spec s;
+    s.cls = CLS_LINEAR;
+    s.A = XN;
+    s.cin = round_up(C, tc ? 64 : 16);
+    s.N = 2 * F;
+    if (pass == 1) {
+      s.W.assign((size_t)s.N * s.cin, 0.0f);
+      pack_linear(s.W, s.cin, 0, b.w1);
+      pack_linear(s.W, s.cin, F, b.wgate);
+    }
+    const bool fuse = tc && F % 16 == 0 && pick_bn(2 * F, 32) != 0;
+    if (fuse) {
+      s.mode = MODE_SWIGLU;
+      Seg g;
+      g.width = 2 * F;
+      g.raw = H;
+      s.segs = {g};
+      gemm(std::move(s));
+    } else {
+      Tensor AG = tensor(R_AG, 2 * F);
+      Seg g;
+      g.width = 2 * F;
+      g.flags = EPI_RAW;
+      g.raw = AG;
+      s.segs = {g};
+      if (F % 16 != 0) fail(KC_ERR_INVALID, "CUDA backend: " + b.name + ": ffn width must be a multiple of 16");
+      gemm(std::move(s));
+      Engine::Impl* Ip = &I;
+      add(CLS_OTHER, [=](cudaStream_t st, int n) {
+        int rows = n * 400;
+        size_t total = (size_t)rows * F;
+        swiglu_kernel<T><<<(unsigned)((total + 255) / 256), 256, 0, st>>>((const T*)AG.p, AG.ld, F, Ip->rowmask, rows,
+                                                                         (T*)H.p, H.ld);
+      });
+    }
+    Spec s2;
+    s2.cls = CLS_LINEAR;
+    s2.A = H;
+    s2.cin = round_up(F, tc ? 64 : 16);
+    s2.N = w16(C);
+    if (pass == 1) {
+      s2.W.assign((size_t)s2.N * s2.cin, 0.0f);
+      pack_linear(s2.W, s2.cin, 0, b.w2);
+    }
+    s2.segs = {close_seg(w16(C), X, XA, next, true)};
+    gemm(std::move(s2));
+  }
+
+  // ---- whole net ----
+  void build_all(OutputLayout& L) {
+    const int C = m.trunk_c;
+    const ConvDesc& ic = m.initial_conv;
+    if (ic.ky != ic.kx) fail(KC_ERR_INVALID, "CUDA backend: non-square initial convolution");
+    stem_k = ic.ky;
+    stem_pad = (ic.ky / 2) * std::max(ic.dy, ic.dx);
+    if (ic.dy != ic.dx) fail(KC_ERR_INVALID, "CUDA backend: anisotropic dilation of the initial convolution");
+    stem_stride = 19 + stem_pad;
+    stem_brows = (19 + stem_pad) * stem_stride;
+    stem_cin = round_up(m.num_input_channels, tc ? 64 : 16);
+    I.stem_rows = round_up(max_batch * stem_brows, 128) + 2 * (stem_pad * stem_stride + stem_pad) + 128;
+
+    Tensor X = tensor(R_LEVEL0, C), XA = tensor(R_LEVEL0 + 1, C);
+    Tensor STEM = tensor(R_STEM, stem_cin);
+    // stem input layout + per-board statistics and trunk bias
+    {
+      const int cin = m.num_input_channels, cpad = stem_cin, brows = stem_brows, stride = stem_stride, pad = stem_pad;
+      Engine::Impl* Ip = &I;
+      add(CLS_OTHER, [=](cudaStream_t st, int n) {
+        prep_input_kernel<T><<<(n * 361 + 127) / 128, 128, 0, st>>>(Ip->in_spatial, n, cin, (T*)STEM.p, STEM.ld, brows,
+                                                                    stride, pad, Ip->rowmask);
+      });
+      (void)cpad;
+      BoardParams bp;
+      std::memset(&bp, 0, sizeof(bp));
+      bp.cin = cin;
+      bp.G = m.num_input_global_channels;
+      bp.wg = up(m.initial_matmul.w);
+      bp.C = C;
+      if (m.has_meta) {
+        bp.m1 = up(m.meta_mul1.w); bp.b1 = up(m.meta_bias1.b); bp.h1 = m.meta_mul1.oc; bp.act1 = m.meta_act1;
+        bp.m2 = up(m.meta_mul2.w); bp.b2 = up(m.meta_bias2.b); bp.h2 = m.meta_mul2.oc; bp.act2 = m.meta_act2;
+        bp.m3 = up(m.meta_mul3.w);
+        if (bp.h1 > 512 || bp.h2 > 512) fail(KC_ERR_INVALID, "CUDA backend: metadata encoder wider than 512");
+      }
+      bp.board_bias = I.board_bias;
+      bp.mask_sum = I.mask_sum;
+      bp.scale1 = I.scale1;
+      bp.scale2 = I.scale2;
+      const bool meta = m.has_meta;
+      add(CLS_OTHER, [=](cudaStream_t st, int n) {
+        BoardParams q = bp;
+        q.spatial = Ip->in_spatial;
+        q.glob = Ip->in_global;
+        q.meta = meta ? Ip->in_meta : nullptr;
+        board_kernel<<<n, 256, 0, st>>>(q);
+      });
+    }
+    // stem conv + per-board bias -> X (remapped into the PBL), XA = first block's pre-BN act
+    {
+      BnAct first = consumer_bn(m.blocks, 0, {});
+      Spec s;
+      s.cls = CLS_STEM;
+      s.A = STEM;
+      s.cin = stem_cin;
+      s.stem = true;
+      s.taps.clear();
+      const int d = std::max(ic.dy, 1);
+      for (int ky = 0; ky < stem_k; ky++)
+        for (int kx = 0; kx < stem_k; kx++)
+          s.taps.push_back(((ky - stem_k / 2) * stem_stride + (kx - stem_k / 2)) * d);
+      s.N = w16(C);
+      const int K = (int)s.taps.size() * s.cin;
+      if (pass == 1) {
+        s.W.assign((size_t)s.N * K, 0.0f);
+        pack_conv(s.W, K, s.cin, 0, ic);
+      }
+      Seg g;
+      g.width = w16(C);
+      g.flags = EPI_BOARD_BIAS | EPI_RAW | (X.f32 ? EPI_RAW_F32 : 0);
+      g.board_bias = I.board_bias;
+      g.ld_bb = C;
+      g.raw = X;
+      if (first.bn) {
+        g.flags |= EPI_ACT;
+        g.act = first.act;
+        g.scale = first.bn->merged_scale;
+        g.bias = first.bn->merged_bias;
+        g.actout = XA;
+      }
+      s.segs = {g};
+      gemm(std::move(s));
+    }
+    // trunk
+    BnAct tip;
+    if (m.trunk_norm_kind == 0) tip = {&m.tip_bn, m.tip_act};
+    emit_stack(m.blocks, 0, C, tip);
+    if (m.trunk_norm_kind != 0) {
+      const float* g = up(m.tip_rms_gamma);
+      const float* bb = up(m.tip_rms_beta);
+      float eps = m.tip_rms_eps;
+      int spatial = m.tip_rms_spatial ? 1 : 0;
+      int act = m.tip_act;
+      Engine::Impl* Ip = &I;
+      add(CLS_OTHER, [=](cudaStream_t st, int n) {
+        if (X.f32)
+          tip_rms_kernel<float, T><<<n, 512, 0, st>>>((const float*)X.p, X.ld, C, g, bb, eps, spatial, act,
+                                                      Ip->rowmask, Ip->mask_sum, (T*)XA.p, XA.ld);
+        else
+          tip_rms_kernel<T, T><<<n, 512, 0, st>>>((const T*)X.p, X.ld, C, g, bb, eps, spatial, act, Ip->rowmask,
+                                                  Ip->mask_sum, (T*)XA.p, XA.ld);
+      });
+    }
+    // heads: one GEMM for p1 | g1 | v1 (bin2onnx.py policy_head :1495, value_head :1518)
+    const int p1c = m.p1_conv.oc, g1c = m.g1_conv.oc, v1c = m.v1_conv.oc;
+    const int P1p = w16(p1c), G1p = w16(g1c), V1p = w16(v1c);
+    Tensor HEAD = tensor(R_HEAD, P1p + G1p + V1p);
+    Tensor P1A = tensor(R_P1A, p1c);
+    {
+      Seg s0;
+      s0.width = P1p;
+      s0.flags = EPI_RAW;
+      s0.raw = HEAD;
+      // HEAD column = GEMM column: each segment's output base is its first GEMM column
+      Seg s1 = act_seg(G1p, m.g1_bn, m.g1_act, HEAD, P1p);
+      Seg s2 = act_seg(V1p, m.v1_bn, m.v1_act, HEAD, P1p + G1p);
+      gemm(conv_spec(CLS_LINEAR, XA, C, {&m.p1_conv, &m.g1_conv, &m.v1_conv}, {s0, s1, s2}));
+    }
+    L.policy_off = 0;
+    L.value_off = m.num_policy_channels * 362;
+    L.score_off = L.value_off + m.num_value_channels();
+    L.own_off = L.score_off + m.num_score_value_channels();
+    L.row_len = L.own_off + 361 * m.num_ownership_channels();
+    const int row_len = L.row_len;
+    float* g1pool = fbuffer(F_POOL, 3 * g1c);
+    float* p1bias = fbuffer(F_GBIAS, p1c);
+    pool(HEAD, P1p, g1c, false, g1pool);
+    fc(g1pool, 3 * g1c, m.gpool_to_bias_mul, nullptr, ACT_IDENTITY, p1bias, p1c, 0, 1);
+    bias_bnact(HEAD, 0, p1bias, m.p1_bn, m.p1_act, p1c, P1A);
+    {
+      // p2 weights [p1c][P] and ownership weights [v1c] (1x1 convs, file order [ic][oc])
+      const float* w2 = up(m.p2_conv.w);
+      const float* wo = up(m.v_ownership_conv.w);
+      const int P = m.num_policy_channels, own_off = L.own_off;
+      const int v1c0 = P1p + G1p;
+      Engine::Impl* Ip = &I;
+      add(CLS_OTHER, [=](cudaStream_t st, int n) {
+        head_spatial_kernel<T><<<(n * 361 + 127) / 128, 128, 0, st>>>((const T*)P1A.p, P1A.ld, p1c, w2, P,
+                                                                     (const T*)HEAD.p, HEAD.ld, v1c0, v1c, wo, Ip->out,
+                                                                     row_len, own_off, n);
+      });
+    }
+    // pass logit: policy[p * 362 + 361]
+    if (m.pass_mlp) {
+      float* tmp = fbuffer(F_PASS, m.gpool_to_pass_mul.oc);
+      fc(g1pool, 3 * g1c, m.gpool_to_pass_mul, &m.gpool_to_pass_bias, m.pass_act, tmp, m.gpool_to_pass_mul.oc, 0, 1);
+      fc(tmp, m.gpool_to_pass_mul.oc, m.gpool_to_pass_mul2, nullptr, ACT_IDENTITY, nullptr, row_len, 361, 362);
+    } else {
+      fc(g1pool, 3 * g1c, m.gpool_to_pass_mul, nullptr, ACT_IDENTITY, nullptr, row_len, 361, 362);
+    }
+    // value head
+    float* vpool = fbuffer(F_VPOOL, 3 * v1c);
+    float* v2 = fbuffer(F_V2, m.v2_mul.oc);
+    pool(HEAD, P1p + G1p, v1c, true, vpool);
+    fc(vpool, 3 * v1c, m.v2_mul, &m.v2_bias, m.v2_act, v2, m.v2_mul.oc, 0, 1);
+    fc(v2, m.v2_mul.oc, m.v3_mul, &m.v3_bias, ACT_IDENTITY, nullptr, row_len, L.value_off, 1);
+    fc(v2, m.v2_mul.oc, m.sv3_mul, &m.sv3_bias, ACT_IDENTITY, nullptr, row_len, L.score_off, 1);
+  }
+};
+
+}  // namespace
+
+Engine::Engine(const ModelDesc& m, int device, int max_batch, int precision)
+    : device_(device), max_batch_(max_batch), precision_(precision), impl_(new Impl) {
+  if (max_batch < 1) fail(KC_ERR_INVALID, "CUDA backend: max batch size must be positive");
+  KC_CUDA(cudaSetDevice(device));
+  Impl& I = *impl_;
+  int dev_sms = 0;
+  KC_CUDA(cudaDeviceGetAttribute(&dev_sms, cudaDevAttrMultiProcessorCount, device));
+  I.sm_count = dev_sms;
+  I.R = round_up(max_batch * 400, 128) + 128;
+  I.d_err = static_cast<int*>(I.alloc(sizeof(int) * 4));
+  I.rowmask = static_cast<float*>(I.alloc((size_t)I.R * sizeof(float)));
+  I.mask_sum = static_cast<float*>(I.alloc((size_t)max_batch * sizeof(float)));
+  I.scale1 = static_cast<float*>(I.alloc((size_t)max_batch * sizeof(float)));
+  I.scale2 = static_cast<float*>(I.alloc((size_t)max_batch * sizeof(float)));
+  I.board_bias = static_cast<float*>(I.alloc((size_t)max_batch * m.trunk_c * sizeof(float)));
+  switch (precision) {
+    case PREC_F32: build_model<float>(m); break;
+    case PREC_F16: build_model<__half>(m); break;
+    case PREC_BF16: build_model<__nv_bfloat16>(m); break;
+    default: fail(KC_ERR_INVALID, "CUDA backend: unknown precision");
+  }
+  KC_CUDA(cudaDeviceSynchronize());
+}
+
+Engine::~Engine() {
+  if (impl_) {
+    cudaSetDevice(device_);
+    cudaDeviceSynchronize();
+  }
+  for (auto e : prof_events_) cudaEventDestroy(e);
+}
+
+template <typename T>
+void Engine::build_model(const ModelDesc& m) {
+  Builder<T> b(*impl_, plan_, m, max_batch_, std::is_same<T, __nv_bfloat16>::value);
+  b.pass = 0;
+  OutputLayout L;
+  b.build_all(L);
+  b.pass = 1;
+  b.allocate();
+  b.build_all(L);
+  layout_ = L;
+}
+
+int Engine::device_error() {
+  int e = 0;
+  KC_CUDA(cudaMemcpy(&e, impl_->d_err, sizeof(int), cudaMemcpyDeviceToHost));
+  return e;
+}
+
+int* Engine::error_word() { return impl_->d_err; }
+
+void Engine::clear_device_error() { KC_CUDA(cudaMemset(impl_->d_err, 0, sizeof(int))); }
+
+void Engine::set_profiling(bool on) {
+  if (on && prof_events_.empty()) {
+    KC_CUDA(cudaSetDevice(device_));
+    prof_events_.resize(2 * plan_.size());
+    for (auto& e : prof_events_) KC_CUDA(cudaEventCreate(&e));
+  }
+  profiling_ = on;
+}
+
+void Engine::reset_profile() {
+  for (int i = 0; i < CLS_COUNT; i++) {
+    prof_ms_[i] = 0;
+    prof_n_[i] = 0;
+  }
+  prof_pending_ = false;
+}
+
+void Engine::collect_profile() {
+  if (!prof_pending_) return;
+  KC_CUDA(cudaEventSynchronize(prof_events_.back()));
+  for (size_t j = 0; j < plan_.size(); j++) {
+    float ms = 0;
+    KC_CUDA(cudaEventElapsedTime(&ms, prof_events_[2 * j], prof_events_[2 * j + 1]));
+    prof_ms_[plan_[j].cls] += ms;
+    prof_n_[plan_[j].cls] += 1;
+  }
+  prof_pending_ = false;
+}
+
+void Engine::profile(double* ms, int64_t* launches, int n) {
+  collect_profile();
+  for (int i = 0; i < n && i < CLS_COUNT; i++) {
+    if (ms) ms[i] = prof_ms_[i];
+    if (launches) launches[i] = prof_n_[i];
+  }
+}
+
+void Engine::run_plan(int n, cudaStream_t stream, bool events) {
+  for (size_t j = 0; j < plan_.size(); j++) {
+    // external event nodes: recorded each time a captured graph runs
+    if (events) KC_CUDA(cudaEventRecordWithFlags(prof_events_[2 * j], stream, cudaEventRecordExternal));
+    plan_[j].fn(stream, n);
+    KC_CUDA(cudaGetLastError());
+    if (events) KC_CUDA(cudaEventRecordWithFlags(prof_events_[2 * j + 1], stream, cudaEventRecordExternal));
+  }
+}
+
+void Engine::forward(int n, cudaStream_t stream, const float* d_spatial, const float* d_global, const float* d_meta,
+                     float* d_out) {
+  if (n < 1 || n > max_batch_)
+    fail(KC_ERR_INVALID, "CUDA backend: batch of " + std::to_string(n) + " rows outside [1, " +
+                             std::to_string(max_batch_) + "]");
+  Impl& I = *impl_;
+  KC_CUDA(cudaSetDevice(device_));
+  if (prof_pending_) collect_profile();
+  I.in_spatial = d_spatial;
+  I.in_global = d_global;
+  I.in_meta = d_meta;
+  I.out = d_out;
+  const bool events = profiling_;
+  if (!use_graphs_) {
+    run_plan(n, stream, events);
+  } else {
+    auto key = std::make_tuple(n * 2 + (events ? 1 : 0), (const void*)d_spatial, (const void*)d_global,
+                               (const void*)d_meta, (void*)d_out);
+    auto it = I.graphs.find(key);
+    if (it == I.graphs.end()) {
+      cudaGraph_t g;
+      KC_CUDA(cudaStreamBeginCapture(stream, cudaStreamCaptureModeThreadLocal));
+      try {
+        run_plan(n, stream, events);
+      } catch (...) {
+        cudaStreamEndCapture(stream, &g);
+        cudaGetLastError();
+        throw;
+      }
+      KC_CUDA(cudaStreamEndCapture(stream, &g));
+      cudaGraphExec_t ge;
+      KC_CUDA(cudaGraphInstantiate(&ge, g, 0));
+      cudaGraphDestroy(g);
+      it = I.graphs.emplace(key, ge).first;
+    }
+    KC_CUDA(cudaGraphLaunch(it->second, stream));
+  }
+  if (events) prof_pending_ = true;
+}
+
+void model_flops(const ModelDesc& m, double* total, double* conv3x3) {
+  const double area = 361;
+  double t = 0, c3 = 0;
+  std::function<void(const std::vector<BlockDesc>&)> walk = [&](const std::vector<BlockDesc>& v) {
+    for (auto& b : v) {
+      auto conv = [&](const ConvDesc& c) {
+        double f = 2.0 * area * c.ky * c.kx * c.ic * c.oc;
+        t += f;
+        if (c.ky == 3) c3 += f;
+      };
+      switch (b.kind) {
+        case BLOCK_ORDINARY: conv(b.regular); conv(b.final_conv); break;
+        case BLOCK_GPOOL: conv(b.regular); conv(b.gpool_conv); conv(b.final_conv); break;
+        case BLOCK_NESTED: conv(b.pre_conv); walk(b.inner); conv(b.post_conv); break;
+        case BLOCK_ATTENTION:
+          t += 2.0 * area * (b.q.ic * (double)b.q.oc + b.k.ic * (double)b.k.oc + b.v.ic * (double)b.v.oc +
+                             b.out.ic * (double)b.out.oc);
+          t += 2.0 * area * area * b.heads * (b.head_dim + b.v_head_dim);
+          break;
+        case BLOCK_FFN: t += 2.0 * area * (b.w1.ic * (double)b.w1.oc * 2 + b.w2.ic * (double)b.w2.oc); break;
+      }
+    }
+  };
+  walk(m.blocks);
+  const ConvDesc& ic = m.initial_conv;
+  t += 2.0 * area * ic.ky * ic.kx * ic.ic * ic.oc;
+  t += 2.0 * area * m.trunk_c * (double)(m.p1_conv.oc + m.g1_conv.oc + m.v1_conv.oc);
+  if (total) *total = t;
+  if (conv3x3) *conv3x3 = c3;
+}
+
+}  // namespace kc

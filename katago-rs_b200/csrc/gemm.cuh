@@ -1,0 +1,544 @@
+// Implicit-GEMM convolutions and token linears of the katago-rs B200 backend.
+//
+// Every 3x3 / 5x5 / 1x1 convolution and every transformer linear of the reference forward pass
+// (tools/bin2onnx/bin2onnx.py GraphBuilder.conv :1140, matmul_tokens :1326) is one GEMM over the board-point rows
+// of an activation tensor in the padded board layout (PBL):
+//
+//   out[r, n] = sum_{tap, c} A[r + tap_off[tap], c] * W[n, tap * cin + c]
+//
+// A is NHWC with one row per point of a 20-column grid per board (19 board columns + 1 zero column shared by the
+// left and right halo) and 20 rows per board (a zero row shared by the boards above and below), so a 3x3 tap is a
+// constant row offset dy*20+dx and the whole convolution is nine shifted row windows of the same tensor: no
+// im2col, no gather. Zero halo rows are maintained by every epilogue (it writes 0 there). The stem reads a
+// 21-column / 2-halo layout built for 5x5 kernels and its epilogue remaps rows into the PBL.
+//
+// Two kernels share the epilogue:
+//  * gemm_tc_kernel (f16 / bf16): persistent, warp-specialised tcgen05 kernel. Warp 0 issues TMA loads of the
+//    A window (128 rows x 64 channels at the tap's row offset) and the weight tile into a STAGES-deep ring,
+//    warp 1 issues tcgen05.mma (M = 128, N = BN, K = 16) into one of two TMEM accumulators, warps 2-5 drain the
+//    other accumulator (tcgen05.ld) through the fused epilogue while the next tile's MMAs run.
+//  * gemm_simt_kernel (f32 parity tier, any type): 64 x 64 register-tiled SIMT GEMM over the same row geometry.
+//
+// Fused epilogue (per row r, column c): + per-board bias (stem: global-feature matmul), x mask (transformer
+// residual branches), + residual, raw output, BN + activation + mask output for the next layer
+// (bin2onnx.py bn_act_mask :1170), or SwiGLU (silu(a) * gate, bin2onnx.py :1433) or 2D RoPE on Q and K
+// (bin2onnx.py rope :1342, applied to the f32 accumulators).
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+
+#include <type_traits>
+
+#include "ptx.cuh"
+
+namespace kc {
+
+enum EpiFlags : int {
+  EPI_BOARD_BIAS = 1,  // acc += board_bias[board][col]
+  EPI_MASK_ACC = 2,    // acc *= mask before the residual add (transformer branch outputs are masked)
+  EPI_RESIDUAL = 4,    // y = acc + residual[row][col]
+  EPI_RAW = 8,         // out_raw[row][col] = y * mask
+  EPI_ACT = 16,        // out_act[row][col] = act(y * scale[col] + bias[col]) * mask
+  EPI_RES_F32 = 32,    // the residual is float32 (the bf16 tier keeps the residual stream in float32)
+  EPI_RAW_F32 = 64,    // the raw output is float32
+};
+
+enum GemmMode : int { MODE_SEGMENTS = 0, MODE_SWIGLU = 1, MODE_ROPE = 2 };
+
+struct EpiSeg {
+  int n0 = 0, n1 = 0;  // GEMM columns [n0, n1) (multiples of 16)
+  int flags = 0, act = 0;
+  const float* scale = nullptr;       // [n1 - n0]
+  const float* bias = nullptr;        // [n1 - n0]
+  const float* board_bias = nullptr;  // [boards][ld_bb]
+  int ld_bb = 0;
+  const void* res = nullptr;
+  int ld_res = 0, res_c0 = 0;
+  void* out_raw = nullptr;
+  int ld_raw = 0, raw_c0 = 0;
+  void* out_act = nullptr;
+  int ld_act = 0, act_c0 = 0;
+};
+
+// Row space of a GEMM: which rows to compute and how a row maps to (board, y, x).
+struct GemmGeom {
+  int rows = 0;        // rows [0, rows) are computed; tiles cover ceil(rows / 128) * 128
+  int board_rows = 400;
+  int stride = 20;     // row within board -> y = rr / stride - pad, x = rr % stride
+  int pad = 1;
+  int remap = 0;       // 1: output row = PBL row of the same (board, y, x) (stem)
+  const float* rowmask = nullptr;  // [PBL rows]: 1 on board, 0 elsewhere
+};
+
+struct GemmParams {
+  GemmGeom g;
+  int n_total = 0;     // N (multiple of the tile width)
+  int cin = 0;         // A channels per tap (multiple of 64 on the tensor-core path)
+  int taps = 1;
+  int tap_off[25] = {0};
+  int mode = MODE_SEGMENTS;
+  int nseg = 1;
+  EpiSeg seg[3];
+  // RoPE (MODE_ROPE): columns [0, rot_cols) are Q then K heads of head_dim, rotated in halves
+  const float* rope_cos = nullptr;  // [tables][361][head_dim/2]
+  const float* rope_sin = nullptr;
+  int rope_table_stride = 0;        // floats between tables (0: one shared table)
+  int rope_q_cols = 0, rope_rot_cols = 0, head_dim = 0, rope_group = 1;
+  int* err = nullptr;
+  // SIMT kernel only
+  const void* a = nullptr;
+  int lda = 0;
+  int a_rows = 0;      // allocated rows of A (rows outside [0, a_rows) read as 0)
+  const void* w = nullptr;  // [n_total][taps * cin]
+};
+
+// ---- element conversions ----
+template <typename T> __device__ __forceinline__ float to_f(T v);
+template <> __device__ __forceinline__ float to_f<float>(float v) { return v; }
+template <> __device__ __forceinline__ float to_f<__half>(__half v) { return __half2float(v); }
+template <> __device__ __forceinline__ float to_f<__nv_bfloat16>(__nv_bfloat16 v) { return __bfloat162float(v); }
+template <typename T> __device__ __forceinline__ T from_f(float v);
+template <> __device__ __forceinline__ float from_f<float>(float v) { return v; }
+template <> __device__ __forceinline__ __half from_f<__half>(float v) { return __float2half_rn(v); }
+template <> __device__ __forceinline__ __nv_bfloat16 from_f<__nv_bfloat16>(float v) { return __float2bfloat16_rn(v); }
+
+// mish(x) = x * tanh(softplus(x)), with tanh(log(1 + e)) = (e^2 + 2e) / (e^2 + 2e + 2), e = exp(x), and the
+// identity above 20 (burn's softplus threshold, crates/katago-nn-burn/src/wino/kernels.rs:131).
+__device__ __forceinline__ float act_apply(float x, int act) {
+  if (act == 1) return fmaxf(x, 0.0f);
+  if (act == 2) {
+    if (x > 20.0f) return x;
+    float e = __expf(x);
+    float n = e * (e + 2.0f);
+    return x * (n / (n + 2.0f));
+  }
+  if (act == 3) return x / (__expf(-x) + 1.0f);
+  return x;
+}
+
+struct RowInfo {
+  int out_row;
+  int board;
+  int pos;      // y * 19 + x
+  float mask;
+  bool write;
+};
+
+__device__ __forceinline__ RowInfo row_info(const GemmGeom& g, int r) {
+  RowInfo ri;
+  int b = r / g.board_rows;
+  int rr = r - b * g.board_rows;
+  int q = rr / g.stride;
+  int yy = q - g.pad;
+  int xx = rr - q * g.stride;
+  bool in_grid = r < g.rows && yy >= 0 && yy < 19 && xx < 19;
+  if (g.remap) {
+    ri.write = in_grid;
+    ri.out_row = in_grid ? b * 400 + (yy + 1) * 20 + xx : 0;
+  } else {
+    ri.write = true;
+    ri.out_row = r;
+  }
+  ri.board = in_grid ? b : 0;
+  ri.pos = in_grid ? yy * 19 + xx : 0;
+  ri.mask = in_grid ? __ldg(g.rowmask + ri.out_row) : 0.0f;
+  return ri;
+}
+
+// Load CNT consecutive T (CNT * sizeof(T) a multiple of 16 bytes, 16-byte aligned) as floats.
+template <typename T, int CNT>
+__device__ __forceinline__ void load_vec(const T* p, float (&v)[CNT]) {
+  static_assert((CNT * sizeof(T)) % 16 == 0, "vector width");
+  constexpr int PER = 16 / sizeof(T);
+#pragma unroll
+  for (int i = 0; i < CNT; i += PER) {
+    uint4 u = *reinterpret_cast<const uint4*>(p + i);
+    const T* e = reinterpret_cast<const T*>(&u);
+#pragma unroll
+    for (int j = 0; j < PER; j++) v[i + j] = to_f<T>(e[j]);
+  }
+}
+
+template <typename T, int CNT>
+__device__ __forceinline__ void store_vec(T* p, const float (&v)[CNT]) {
+  constexpr int PER = 16 / sizeof(T);
+#pragma unroll
+  for (int i = 0; i < CNT; i += PER) {
+    uint4 u;
+    T* e = reinterpret_cast<T*>(&u);
+#pragma unroll
+    for (int j = 0; j < PER; j++) e[j] = from_f<T>(v[i + j]);
+    *reinterpret_cast<uint4*>(p + i) = u;
+  }
+}
+
+template <typename T, int CNT>
+__device__ __forceinline__ void store_zero(T* p) {
+  constexpr int PER = 16 / sizeof(T);
+#pragma unroll
+  for (int i = 0; i < CNT; i += PER) *reinterpret_cast<uint4*>(p + i) = make_uint4(0, 0, 0, 0);
+}
+
+// Segment epilogue for CNT consecutive columns [col0, col0 + CNT) of one row (all in one segment).
+template <typename T, int CNT>
+__device__ __forceinline__ void epi_segment(const GemmParams& p, const RowInfo& ri, int col0, float (&v)[CNT]) {
+  if (!ri.write) return;
+  const EpiSeg* s = &p.seg[0];
+  if (p.nseg > 1 && col0 >= p.seg[0].n1) s = &p.seg[1];
+  if (p.nseg > 2 && col0 >= p.seg[1].n1) s = &p.seg[2];
+  const int c = col0 - s->n0;
+  const int f = s->flags;
+  const float m = ri.mask;
+  if ((f & EPI_BOARD_BIAS) && m != 0.0f) {
+    const float* bb = s->board_bias + (size_t)ri.board * s->ld_bb + c;
+#pragma unroll
+    for (int i = 0; i < CNT; i++) v[i] += __ldg(bb + i);
+  }
+  if (f & EPI_MASK_ACC) {
+#pragma unroll
+    for (int i = 0; i < CNT; i++) v[i] *= m;
+  }
+  if (f & EPI_RESIDUAL) {
+    float rv[CNT];
+    const size_t off = (size_t)ri.out_row * s->ld_res + s->res_c0 + c;
+    if (f & EPI_RES_F32) load_vec<float, CNT>(reinterpret_cast<const float*>(s->res) + off, rv);
+    else load_vec<T, CNT>(reinterpret_cast<const T*>(s->res) + off, rv);
+#pragma unroll
+    for (int i = 0; i < CNT; i++) v[i] += rv[i];
+  }
+  if (f & EPI_RAW) {
+    float o[CNT];
+#pragma unroll
+    for (int i = 0; i < CNT; i++) o[i] = v[i] * m;
+    const size_t off = (size_t)ri.out_row * s->ld_raw + s->raw_c0 + c;
+    if (f & EPI_RAW_F32) store_vec<float, CNT>(reinterpret_cast<float*>(s->out_raw) + off, o);
+    else store_vec<T, CNT>(reinterpret_cast<T*>(s->out_raw) + off, o);
+  }
+  if (f & EPI_ACT) {
+    float o[CNT];
+    if (m != 0.0f) {
+#pragma unroll
+      for (int i = 0; i < CNT; i++) {
+        float t = v[i] * __ldg(s->scale + c + i);
+        t = t + __ldg(s->bias + c + i);
+        o[i] = act_apply(t, s->act) * m;
+      }
+    } else {
+#pragma unroll
+      for (int i = 0; i < CNT; i++) o[i] = 0.0f;
+    }
+    store_vec<T, CNT>(reinterpret_cast<T*>(s->out_act) + (size_t)ri.out_row * s->ld_act + s->act_c0 + c, o);
+  }
+}
+
+// ================================================================================================================
+// tcgen05 persistent kernel
+// ================================================================================================================
+
+template <int BN>
+struct TcCfg {
+  static constexpr int A_BYTES = 128 * 64 * 2;
+  static constexpr int B_BYTES = BN * 64 * 2;
+  static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+  static constexpr int STAGES = (200 * 1024) / STAGE_BYTES > 8 ? 8 : (200 * 1024) / STAGE_BYTES;
+  static constexpr uint32_t ACC_COLS = BN <= 32 ? 32 : BN <= 64 ? 64 : BN <= 128 ? 128 : 256;
+  static constexpr uint32_t TMEM_COLS = 2 * ACC_COLS;
+  static constexpr int BAR_BYTES = 256;
+  static constexpr int SMEM = 1024 /*align slack*/ + STAGES * STAGE_BYTES + BAR_BYTES;
+  static constexpr int THREADS = 192;
+};
+
+template <typename T, int BN>
+__device__ __forceinline__ void tc_epilogue_tile(const GemmParams& p, uint32_t tacc, int m0, int n0, int row_in_tile) {
+  const RowInfo ri = row_info(p.g, m0 + row_in_tile);
+  if (p.mode == MODE_SEGMENTS) {
+#pragma unroll 1
+    for (int c = 0; c < BN; c += 16) {
+      uint32_t u[16];
+      tmem_ld16(tacc + c, u);
+      tmem_wait_ld();
+      float v[16];
+#pragma unroll
+      for (int i = 0; i < 16; i++) v[i] = __uint_as_float(u[i]);
+      epi_segment<T, 16>(p, ri, n0 + c, v);
+    }
+  } else if (p.mode == MODE_SWIGLU) {
+    const EpiSeg& s = p.seg[0];
+#pragma unroll 1
+    for (int c = 0; c < BN / 2; c += 16) {
+      uint32_t ua[16], ug[16];
+      tmem_ld16(tacc + c, ua);
+      tmem_ld16(tacc + BN / 2 + c, ug);
+      tmem_wait_ld();
+      float h[16];
+#pragma unroll
+      for (int i = 0; i < 16; i++) {
+        float a = __uint_as_float(ua[i]);
+        float g = __uint_as_float(ug[i]);
+        h[i] = (a / (__expf(-a) + 1.0f)) * g * ri.mask;
+      }
+      if (ri.write)
+        store_vec<T, 16>(reinterpret_cast<T*>(s.out_raw) + (size_t)ri.out_row * s.ld_raw + n0 / 2 + c, h);
+    }
+  } else {  // MODE_ROPE: Q|K|V columns, Q and K heads rotated in halves of head_dim / 2
+    const EpiSeg& s = p.seg[0];
+    const int hd = p.head_dim, half = hd / 2;
+#pragma unroll 1
+    for (int c = 0; c < BN; c += 16) {
+      const int gcol = n0 + c;
+      if (gcol < p.rope_rot_cols) {
+        const int within = gcol % hd;
+        if (within >= half) continue;  // written with its pair
+        uint32_t u0[16], u1[16];
+        tmem_ld16(tacc + c, u0);
+        tmem_ld16(tacc + c + half, u1);
+        tmem_wait_ld();
+        const int head = gcol / hd;
+        int table;
+        if (gcol < p.rope_q_cols) table = head / p.rope_group;
+        else table = head - p.rope_q_cols / hd;
+        const float* ct = p.rope_cos + (size_t)table * p.rope_table_stride + (size_t)ri.pos * half + within;
+        const float* st = p.rope_sin + (size_t)table * p.rope_table_stride + (size_t)ri.pos * half + within;
+        float r0[16], r1[16];
+#pragma unroll
+        for (int i = 0; i < 16; i++) {
+          float x0 = __uint_as_float(u0[i]), x1 = __uint_as_float(u1[i]);
+          float cs = __ldg(ct + i), sn = __ldg(st + i);
+          r0[i] = (x0 * cs - x1 * sn) * ri.mask;
+          r1[i] = (x0 * sn + x1 * cs) * ri.mask;
+        }
+        if (ri.write) {
+          T* o = reinterpret_cast<T*>(s.out_raw) + (size_t)ri.out_row * s.ld_raw + gcol;
+          store_vec<T, 16>(o, r0);
+          store_vec<T, 16>(o + half, r1);
+        }
+      } else {
+        uint32_t u[16];
+        tmem_ld16(tacc + c, u);
+        tmem_wait_ld();
+        float v[16];
+#pragma unroll
+        for (int i = 0; i < 16; i++) v[i] = __uint_as_float(u[i]) * ri.mask;
+        if (ri.write) store_vec<T, 16>(reinterpret_cast<T*>(s.out_raw) + (size_t)ri.out_row * s.ld_raw + gcol, v);
+      }
+    }
+  }
+}
+
+template <typename T, int BN>
+__global__ void __launch_bounds__(192, 1)
+    gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                   const __grid_constant__ GemmParams p) {
+  using C = TcCfg<BN>;
+  constexpr int fmt = sizeof(T) == 2 && std::is_same<T, __nv_bfloat16>::value ? 1 : 0;
+  constexpr uint32_t IDESC = make_idesc_f16(fmt, 128, BN);
+
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + C::STAGES * C::STAGE_BYTES);
+  uint64_t* empty = full + C::STAGES;
+  uint64_t* tfull = empty + C::STAGES;
+  uint64_t* tempty = tfull + 2;
+  uint64_t* drain = tempty + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int m_tiles = (p.g.rows + 127) / 128;
+  const int n_tiles = p.n_total / BN;
+  const int num_tiles = m_tiles * n_tiles;
+  const int kb_per_tap = p.cin / 64;
+  const int KB = p.taps * kb_per_tap;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < C::STAGES; s++) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int a = 0; a < 2; a++) {
+      mbar_init(&tfull[a], 1);
+      mbar_init(&tempty[a], 128);
+    }
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+    prefetch_tensormap(&tmA);
+    prefetch_tensormap(&tmB);
+  }
+  if (warp == 0) {
+    tmem_alloc(tmem_slot, C::TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ---- TMA producer ----
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
+        const int m0 = (tile / n_tiles) * 128;
+        const int n0 = (tile % n_tiles) * BN;
+        for (int kb = 0; kb < KB; kb++) {
+          if (!mbar_wait(&empty[stage], phase ^ 1, p.err, DEV_TIMEOUT_PRODUCER) || *abort_flag) {
+            ok = false;
+            *abort_flag = 1;
+            break;
+          }
+          const int tap = kb / kb_per_tap;
+          const int c0 = (kb - tap * kb_per_tap) * 64;
+          uint8_t* sa = smem + stage * C::STAGE_BYTES;
+          mbar_expect_tx(&full[stage], C::STAGE_BYTES);
+          tma_load_2d(sa, &tmA, &full[stage], c0, m0 + p.tap_off[tap]);
+          tma_load_2d(sa + C::A_BYTES, &tmB, &full[stage], kb * 64, n0);
+          if (++stage == C::STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+      }
+      if (!ok) {
+        // let copies already issued land before the CTA exits (bounded)
+        unsigned long long t0 = globaltimer();
+        while (globaltimer() - t0 < 2000000ull) {
+        }
+      }
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    if (lane == 0) {
+      // ---- MMA issuer ----
+      int stage = 0;
+      uint32_t phase = 0;
+      int local = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x, local++) {
+        const int acc = local & 1;
+        const uint32_t acc_phase = (local >> 1) & 1;
+        if (!mbar_wait(&tempty[acc], acc_phase ^ 1, p.err, DEV_TIMEOUT_MMA) || *abort_flag) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + acc * C::ACC_COLS;
+        for (int kb = 0; kb < KB; kb++) {
+          if (!mbar_wait(&full[stage], phase, p.err, DEV_TIMEOUT_MMA) || *abort_flag) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t sa = smem_u32(smem + stage * C::STAGE_BYTES);
+          const uint32_t sb = sa + C::A_BYTES;
+#pragma unroll
+          for (int k = 0; k < 4; k++)
+            umma_f16(d_tmem, make_sw128_desc(sa + k * 32), make_sw128_desc(sb + k * 32), IDESC, (kb | k) != 0);
+          umma_commit(&empty[stage]);
+          if (++stage == C::STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+        if (!ok) break;
+        umma_commit(&tfull[acc]);
+      }
+      if (!ok) {
+        *abort_flag = 1;
+        umma_commit(drain);  // wait for MMAs in flight before TMEM is released
+        mbar_wait(drain, 0, p.err, DEV_TIMEOUT_DRAIN);
+      }
+    }
+    __syncwarp();
+  } else {
+    // ---- epilogue warps 2..5: TMEM lane quarter = warp % 4 ----
+    const int q = warp & 3;
+    const int row_in_tile = q * 32 + lane;
+    int local = 0;
+    for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, local++) {
+      const int acc = local & 1;
+      const uint32_t acc_phase = (local >> 1) & 1;
+      if (!mbar_wait(&tfull[acc], acc_phase, p.err, DEV_TIMEOUT_EPILOGUE) || *abort_flag) {
+        *abort_flag = 1;
+        break;
+      }
+      __syncwarp();
+      tc_fence_after();
+      const int m0 = (tile / n_tiles) * 128;
+      const int n0 = (tile % n_tiles) * BN;
+      const uint32_t tacc = tmem_base + acc * C::ACC_COLS + ((uint32_t)(q * 32) << 16);
+      tc_epilogue_tile<T, BN>(p, tacc, m0, n0, row_in_tile);
+      tc_fence_before();
+      mbar_arrive(&tempty[acc]);
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, C::TMEM_COLS);
+  }
+}
+
+// ================================================================================================================
+// SIMT kernel (the f32 tier): 64 x 64 tile, 256 threads, 4 x 4 per thread, K chunks of 16
+// ================================================================================================================
+
+template <typename T>
+__global__ void __launch_bounds__(256) gemm_simt_kernel(const __grid_constant__ GemmParams p) {
+  static_assert(sizeof(T) == 4, "the SIMT GEMM is the float32 path");
+  __shared__ float As[16][64 + 4];
+  __shared__ float Ws[16][64 + 4];
+  const int tx = threadIdx.x & 15, ty = threadIdx.x >> 4;
+  const int m0 = blockIdx.x * 64, n0 = blockIdx.y * 64;
+  const T* A = reinterpret_cast<const T*>(p.a);
+  const T* W = reinterpret_cast<const T*>(p.w);
+  const int K = p.taps * p.cin;
+  float acc[4][4] = {};
+  for (int tap = 0; tap < p.taps; tap++) {
+    const int off = p.tap_off[tap];
+    for (int c0 = 0; c0 < p.cin; c0 += 16) {
+      // A tile: 64 rows x 16 channels; W tile: 64 columns x 16 k
+      for (int i = threadIdx.x; i < 64 * 16; i += 256) {
+        const int rr = i >> 4, kk = i & 15;
+        const int ra = m0 + rr + off;
+        const int cc = c0 + kk;
+        float av = 0.0f;
+        if (ra >= 0 && ra < p.a_rows && cc < p.cin) av = to_f<T>(A[(size_t)ra * p.lda + cc]);
+        As[kk][rr] = av;
+        const int n = n0 + rr;
+        float wv = 0.0f;
+        if (n < p.n_total && cc < p.cin) wv = to_f<T>(W[(size_t)n * K + tap * p.cin + cc]);
+        Ws[kk][rr] = wv;
+      }
+      __syncthreads();
+#pragma unroll
+      for (int kk = 0; kk < 16; kk++) {
+        float a[4], w[4];
+#pragma unroll
+        for (int i = 0; i < 4; i++) a[i] = As[kk][ty * 4 + i];
+#pragma unroll
+        for (int j = 0; j < 4; j++) w[j] = Ws[kk][tx * 4 + j];
+#pragma unroll
+        for (int i = 0; i < 4; i++)
+#pragma unroll
+          for (int j = 0; j < 4; j++) acc[i][j] = fmaf(a[i], w[j], acc[i][j]);
+      }
+      __syncthreads();
+    }
+  }
+  const int ncol = n0 + tx * 4;
+  if (ncol >= p.n_total) return;
+#pragma unroll
+  for (int i = 0; i < 4; i++) {
+    const int r = m0 + ty * 4 + i;
+    const RowInfo ri = row_info(p.g, r);
+    float v[4] = {acc[i][0], acc[i][1], acc[i][2], acc[i][3]};
+    epi_segment<T, 4>(p, ri, ncol, v);
+  }
+}
+
+}  // namespace kc

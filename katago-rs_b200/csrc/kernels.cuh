@@ -1,0 +1,397 @@
+// Memory-bound kernels of the katago-rs B200 forward pass: input layout conversion, per-board statistics and
+// biases, masked global pooling, the small head matmuls, batch-norm/RMSNorm elementwise passes, and the SIMT
+// attention / RoPE / SwiGLU paths of the float32 tier. Semantics follow tools/bin2onnx/bin2onnx.py GraphBuilder
+// (line numbers on each kernel).
+#pragma once
+
+#include "gemm.cuh"
+
+namespace kc {
+
+// Positions of a board in the padded board layout (PBL): row of (b, y, x) = b * 400 + (y + 1) * 20 + x.
+__host__ __device__ __forceinline__ int pbl_row(int b, int y, int x) { return b * 400 + (y + 1) * 20 + x; }
+
+// ---------------------------------------------------------------------------------------------------------------
+// Input: NCHW float32 [n][cin][19*19] -> stem layout T rows [b * brows + (y + pad) * stride + x][cpad], and the
+// per-PBL-row on-board mask (input channel 0, bin2onnx.py setup_mask :1203-1206).
+// ---------------------------------------------------------------------------------------------------------------
+template <typename T>
+__global__ void prep_input_kernel(const float* __restrict__ in, int n, int cin, T* __restrict__ out, int cpad,
+                                  int brows, int stride, int pad, float* __restrict__ rowmask) {
+  int idx = blockIdx.x * blockDim.x + threadIdx.x;
+  if (idx >= n * 361) return;
+  int b = idx / 361, pos = idx - b * 361;
+  int y = pos / 19, x = pos - y * 19;
+  const float* src = in + (size_t)b * cin * 361 + pos;
+  T* dst = out + ((size_t)b * brows + (size_t)(y + pad) * stride + x) * cpad;
+  for (int c = 0; c < cin; c++) dst[c] = from_f<T>(__ldg(src + (size_t)c * 361));
+  for (int c = cin; c < cpad; c++) dst[c] = from_f<T>(0.0f);
+  rowmask[pbl_row(b, y, x)] = __ldg(src);
+}
+
+// ---------------------------------------------------------------------------------------------------------------
+// Per board: mask sum and the pooling scales (bin2onnx.py setup_mask :1207-1215), and the trunk's per-board bias:
+// global features x initial matmul, plus the SGF-metadata encoder for human-SL nets (bin2onnx.py :1467-1487).
+// ---------------------------------------------------------------------------------------------------------------
+struct BoardParams {
+  const float* spatial;  // [n][cin][361] (channel 0 = mask)
+  int cin;
+  const float* glob;     // [n][G]
+  int G;
+  const float* wg;       // [G][C]
+  int C;
+  const float* meta;     // [n][192] or null
+  const float* m1; const float* b1; int h1; int act1;   // [192][h1]
+  const float* m2; const float* b2; int h2; int act2;   // [h1][h2]
+  const float* m3;                                      // [h2][C]
+  float* board_bias;     // [n][C]
+  float* mask_sum;       // [n]
+  float* scale1;         // [n]
+  float* scale2;         // [n]
+};
+
+__global__ void board_kernel(const __grid_constant__ BoardParams p) {
+  __shared__ float red[256];
+  __shared__ float hbuf[2][512];
+  const int b = blockIdx.x;
+  float s = 0.0f;
+  for (int i = threadIdx.x; i < 361; i += blockDim.x) s += p.spatial[(size_t)b * p.cin * 361 + i];
+  red[threadIdx.x] = s;
+  __syncthreads();
+  for (int w = blockDim.x / 2; w > 0; w >>= 1) {
+    if (threadIdx.x < w) red[threadIdx.x] += red[threadIdx.x + w];
+    __syncthreads();
+  }
+  if (threadIdx.x == 0) {
+    float ms = red[0];
+    float cen = sqrtf(ms) - 14.0f;
+    p.mask_sum[b] = ms;
+    p.scale1[b] = cen * 0.1f;
+    float sq = cen * cen;
+    sq = sq * 0.01f;
+    p.scale2[b] = sq - 0.1f;
+  }
+  if (p.meta) {
+    const float* mi = p.meta + (size_t)b * 192;
+    for (int o = threadIdx.x; o < p.h1; o += blockDim.x) {
+      float a = 0.0f;
+      for (int i = 0; i < 192; i++) a += mi[i] * p.m1[(size_t)i * p.h1 + o];
+      hbuf[0][o] = act_apply(a + p.b1[o], p.act1);
+    }
+    __syncthreads();
+    for (int o = threadIdx.x; o < p.h2; o += blockDim.x) {
+      float a = 0.0f;
+      for (int i = 0; i < p.h1; i++) a += hbuf[0][i] * p.m2[(size_t)i * p.h2 + o];
+      hbuf[1][o] = act_apply(a + p.b2[o], p.act2);
+    }
+    __syncthreads();
+  }
+  for (int c = threadIdx.x; c < p.C; c += blockDim.x) {
+    float a = 0.0f;
+    for (int i = 0; i < p.G; i++) a += p.glob[(size_t)b * p.G + i] * p.wg[(size_t)i * p.C + c];
+    if (p.meta) {
+      float m = 0.0f;
+      for (int i = 0; i < p.h2; i++) m += hbuf[1][i] * p.m3[(size_t)i * p.C + c];
+      a = a + m;
+    }
+    p.board_bias[(size_t)b * p.C + c] = a;
+  }
+}
+
+// ---------------------------------------------------------------------------------------------------------------
+// Masked pooling over a board's 361 points of channels [c0, c0 + C) of a PBL tensor (already masked):
+// gpool (bin2onnx.py :1222-1230): [mean, mean * scale1, max(x + (mask * 1e4 - 1e4))];
+// value (bin2onnx.py :1232-1239): [mean, mean * scale1, mean * scale2]. out [n][3C] float32.
+// grid (n, ceil(C / 32)), block (32, 8).
+// ---------------------------------------------------------------------------------------------------------------
+template <typename T>
+__global__ void pool_kernel(const T* __restrict__ x, int ld, int c0, int C, const float* __restrict__ rowmask,
+                            const float* __restrict__ mask_sum, const float* __restrict__ scale1,
+                            const float* __restrict__ scale2, int value_mode, float* __restrict__ out) {
+  __shared__ float ssum[8][32], smax[8][32];
+  const int b = blockIdx.x;
+  const int c = blockIdx.y * 32 + threadIdx.x;
+  float s = 0.0f, mx = -INFINITY;
+  if (c < C) {
+    for (int pos = threadIdx.y; pos < 361; pos += 8) {
+      int y = pos / 19, xx = pos - y * 19;
+      int r = pbl_row(b, y, xx);
+      float v = to_f<T>(x[(size_t)r * ld + c0 + c]);
+      s += v;
+      float m = __ldg(rowmask + r);
+      float biasv = m * 1e4f - 1e4f;
+      mx = fmaxf(mx, v + biasv);
+    }
+  }
+  ssum[threadIdx.y][threadIdx.x] = s;
+  smax[threadIdx.y][threadIdx.x] = mx;
+  __syncthreads();
+  if (threadIdx.y == 0 && c < C) {
+    for (int i = 1; i < 8; i++) {
+      s += ssum[i][threadIdx.x];
+      mx = fmaxf(mx, smax[i][threadIdx.x]);
+    }
+    float mean = s / mask_sum[b];
+    float* o = out + (size_t)b * 3 * C;
+    o[c] = mean;
+    o[C + c] = mean * scale1[b];
+    o[2 * C + c] = value_mode ? mean * scale2[b] : mx;
+  }
+}
+
+// ---------------------------------------------------------------------------------------------------------------
+// Small per-board matmul: out[b][off + o * ostride] = act(sum_i in[b][i] * W[i][o] (+ bias[o])).
+// grid n, block 128.
+// ---------------------------------------------------------------------------------------------------------------
+__global__ void fc_kernel(const float* __restrict__ in, int in_ld, int ic, const float* __restrict__ w, int oc,
+                          const float* __restrict__ bias, int act, float* __restrict__ out, int out_ld, int out_off,
+                          int out_stride) {
+  extern __shared__ float xin[];
+  const int b = blockIdx.x;
+  for (int i = threadIdx.x; i < ic; i += blockDim.x) xin[i] = in[(size_t)b * in_ld + i];
+  __syncthreads();
+  for (int o = threadIdx.x; o < oc; o += blockDim.x) {
+    float a = 0.0f;
+    for (int i = 0; i < ic; i++) a += xin[i] * __ldg(w + (size_t)i * oc + o);
+    if (bias) a = a + bias[o];
+    out[(size_t)b * out_ld + out_off + (size_t)o * out_stride] = act_apply(a, act);
+  }
+}
+
+// ---------------------------------------------------------------------------------------------------------------
+// y[r][c] = act((x[r][xc0 + c] (+ board_bias[b][c])) * scale[c] + bias[c]) * mask[r]  for c < C;
+// the gpool-biased regular branch (bin2onnx.py :1256-1258), the policy head's p1 (:1503-1504), and the standalone
+// bn_act_mask (:1170) where a producer could not fuse it. Rows [0, rows); y's channels [C, Cw) are written as 0.
+// ---------------------------------------------------------------------------------------------------------------
+template <typename T>
+__global__ void bias_bnact_kernel(const T* __restrict__ x, int xld, int xc0, const float* __restrict__ board_bias,
+                                  const float* __restrict__ scale, const float* __restrict__ bias, int act,
+                                  const float* __restrict__ rowmask, int rows, int C, int Cw, T* __restrict__ y,
+                                  int yld) {
+  size_t idx = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (idx >= (size_t)rows * Cw) return;
+  int r = (int)(idx / Cw), c = (int)(idx - (size_t)r * Cw);
+  float m = rowmask[r];
+  float o = 0.0f;
+  if (c < C && m != 0.0f) {
+    float v = to_f<T>(x[(size_t)r * xld + xc0 + c]);
+    if (board_bias) v = v + board_bias[(size_t)(r / 400) * C + c];
+    float t = v * scale[c];
+    t = t + bias[c];
+    o = act_apply(t, act) * m;
+  }
+  y[(size_t)r * yld + c] = from_f<T>(o);
+}
+
+// ---------------------------------------------------------------------------------------------------------------
+// Transformer RMSNorm per row (bin2onnx.py transformer_rmsnorm :1330-1340): x * (1 / sqrt(sum(x^2) / C + eps)) * w
+// * mask. One warp per row.
+// ---------------------------------------------------------------------------------------------------------------
+template <typename TI, typename T>
+__global__ void rmsnorm_kernel(const TI* __restrict__ x, int ld, int C, const float* __restrict__ w, float eps,
+                               const float* __restrict__ rowmask, int rows, T* __restrict__ y, int yld) {
+  int r = blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
+  int lane = threadIdx.x & 31;
+  if (r >= rows) return;
+  const TI* xr = x + (size_t)r * ld;
+  float ss = 0.0f;
+  for (int c = lane; c < C; c += 32) {
+    float v = to_f<TI>(xr[c]);
+    ss += v * v;
+  }
+  for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+  float ms = ss / (float)C;
+  float den = sqrtf(ms + eps);
+  float rms = 1.0f / den;
+  float m = rowmask[r];
+  T* yr = y + (size_t)r * yld;
+  for (int c = lane; c < C; c += 32) yr[c] = from_f<T>(to_f<TI>(xr[c]) * rms * w[c] * m);
+}
+
+// ---------------------------------------------------------------------------------------------------------------
+// Trunk-tip RMSNorm (bin2onnx.py trunk_tip_rmsnorm :1440-1463): act(x * rms * gamma + beta) * mask, rms per point
+// over channels, or (spatial) one rms per board over channels x on-board points. One block per board.
+// ---------------------------------------------------------------------------------------------------------------
+template <typename TI, typename T>
+__global__ void tip_rms_kernel(const TI* __restrict__ x, int ld, int C, const float* __restrict__ gamma,
+                               const float* __restrict__ beta, float eps, int spatial, int act,
+                               const float* __restrict__ rowmask, const float* __restrict__ mask_sum,
+                               T* __restrict__ y, int yld) {
+  __shared__ float rms_s[361];
+  __shared__ float red[32];
+  const int b = blockIdx.x;
+  const int warp = threadIdx.x / 32, lane = threadIdx.x & 31, nw = blockDim.x / 32;
+  for (int pos = warp; pos < 361; pos += nw) {
+    int r = pbl_row(b, pos / 19, pos % 19);
+    float ss = 0.0f;
+    for (int c = lane; c < C; c += 32) {
+      float v = to_f<TI>(x[(size_t)r * ld + c]);
+      ss += v * v;
+    }
+    for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+    if (lane == 0) rms_s[pos] = spatial ? ss * rowmask[r] : ss;
+  }
+  __syncthreads();
+  if (spatial) {
+    float s = 0.0f;
+    for (int pos = threadIdx.x; pos < 361; pos += blockDim.x) s += rms_s[pos];
+    for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+    if (lane == 0) red[warp] = s;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      float t = 0.0f;
+      for (int i = 0; i < nw; i++) t += red[i];
+      float count = mask_sum[b] * (float)C;
+      float ms = t / count;
+      red[0] = 1.0f / sqrtf(ms + eps);
+    }
+    __syncthreads();
+    float rr = red[0];
+    __syncthreads();
+    for (int pos = threadIdx.x; pos < 361; pos += blockDim.x) rms_s[pos] = rr;
+  } else {
+    __syncthreads();
+    for (int pos = threadIdx.x; pos < 361; pos += blockDim.x) {
+      float ms = rms_s[pos] / (float)C;
+      rms_s[pos] = 1.0f / sqrtf(ms + eps);
+    }
+  }
+  __syncthreads();
+  for (int pos = warp; pos < 361; pos += nw) {
+    int r = pbl_row(b, pos / 19, pos % 19);
+    float m = rowmask[r], rr = rms_s[pos];
+    for (int c = lane; c < C; c += 32) {
+      float v = to_f<TI>(x[(size_t)r * ld + c]) * rr;
+      v = v * gamma[c];
+      v = v + beta[c];
+      y[(size_t)r * yld + c] = from_f<T>(act_apply(v, act) * m);
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------------------------------------------
+// Policy p2 (1x1 conv p1 -> P, bin2onnx.py :1505) and ownership (1x1 conv v1 -> 1, :1530) per board point, written
+// into the output rows: policy[p * 362 + pos], ownership[own_off + pos]. One thread per (board, point).
+// ---------------------------------------------------------------------------------------------------------------
+template <typename T>
+__global__ void head_spatial_kernel(const T* __restrict__ p1a, int p1ld, int p1c, const float* __restrict__ w2,
+                                    int P, const T* __restrict__ v1a, int v1ld, int v1c0, int v1c,
+                                    const float* __restrict__ wown, float* __restrict__ out, int row_len, int own_off,
+                                    int n) {
+  int idx = blockIdx.x * blockDim.x + threadIdx.x;
+  if (idx >= n * 361) return;
+  int b = idx / 361, pos = idx - b * 361;
+  int r = pbl_row(b, pos / 19, pos % 19);
+  float* o = out + (size_t)b * row_len;
+  for (int p = 0; p < P; p++) {
+    float a = 0.0f;
+    for (int c = 0; c < p1c; c++) a += to_f<T>(p1a[(size_t)r * p1ld + c]) * __ldg(w2 + (size_t)c * P + p);
+    o[p * 362 + pos] = a;
+  }
+  float a = 0.0f;
+  for (int c = 0; c < v1c; c++) a += to_f<T>(v1a[(size_t)r * v1ld + v1c0 + c]) * __ldg(wown + c);
+  o[own_off + pos] = a;
+}
+
+// ---------------------------------------------------------------------------------------------------------------
+// float32-tier RoPE (in place on the QKV buffer) and SwiGLU, where the GEMM epilogue does not fuse them.
+// Q columns [0, qc), K columns [qc, qc + kc); head h's channels are [x0 of each pair..., x1 of each pair...]
+// (the projection columns are permuted so, bin2onnx.py :1369-1374). Tables [tables][361][hd/2].
+// ---------------------------------------------------------------------------------------------------------------
+template <typename T>
+__global__ void rope_kernel(T* __restrict__ qkv, int ld, int qc, int kc, int hd, const float* __restrict__ cosv,
+                            const float* __restrict__ sinv, int table_stride, int group, int rows) {
+  const int half = hd / 2;
+  const int pairs_per_row = (qc + kc) / 2;
+  size_t idx = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (idx >= (size_t)rows * pairs_per_row) return;
+  int r = (int)(idx / pairs_per_row), pr = (int)(idx - (size_t)r * pairs_per_row);
+  int head = pr / half, j = pr - head * half;
+  int rr = r % 400, yy = rr / 20 - 1, xx = rr % 20;
+  if (yy < 0 || xx >= 19) return;
+  int pos = yy * 19 + xx;
+  int qheads = qc / hd;
+  int table = head < qheads ? head / group : head - qheads;
+  float c = cosv[(size_t)table * table_stride + (size_t)pos * half + j];
+  float s = sinv[(size_t)table * table_stride + (size_t)pos * half + j];
+  T* base = qkv + (size_t)r * ld + head * hd;
+  float x0 = to_f<T>(base[j]), x1 = to_f<T>(base[j + half]);
+  float a0 = x0 * c, b1 = x1 * s;
+  float c0 = x0 * s, d1 = x1 * c;
+  base[j] = from_f<T>(a0 - b1);
+  base[j + half] = from_f<T>(c0 + d1);
+}
+
+template <typename T>
+__global__ void swiglu_kernel(const T* __restrict__ ag, int ld, int F, const float* __restrict__ rowmask, int rows,
+                              T* __restrict__ h, int hld) {
+  size_t idx = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (idx >= (size_t)rows * F) return;
+  int r = (int)(idx / F), j = (int)(idx - (size_t)r * F);
+  float a = to_f<T>(ag[(size_t)r * ld + j]);
+  float g = to_f<T>(ag[(size_t)r * ld + F + j]);
+  float s = a / (expf(-a) + 1.0f);
+  h[(size_t)r * hld + j] = from_f<T>(s * g * rowmask[r]);
+}
+
+// ---------------------------------------------------------------------------------------------------------------
+// SIMT attention (bin2onnx.py transformer_attention_block :1359-1423 after the projections): per board and head,
+// softmax(q k^T * scale + bias) v over the board's 361 points, bias = mask * 3e4 - 3e4 (:1313-1323), GQA kv head =
+// h / (heads / kv_heads). One thread per query with an online softmax; K and V of the board staged in shared
+// memory. grid (ceil(400 / 128), heads, n), block 128.
+// ---------------------------------------------------------------------------------------------------------------
+template <typename T, int HD>
+__global__ void __launch_bounds__(128) attention_simt_kernel(const T* __restrict__ qkv, int ld, int qc, int kc,
+                                                             int heads, int kv_heads, float scale,
+                                                             const float* __restrict__ rowmask, T* __restrict__ out,
+                                                             int out_ld) {
+  extern __shared__ uint8_t sm[];
+  T* Ks = reinterpret_cast<T*>(sm);
+  T* Vs = Ks + 361 * HD;
+  float* kb = reinterpret_cast<float*>(Vs + 361 * HD);
+  const int b = blockIdx.z, h = blockIdx.y;
+  const int kvh = h / (heads / kv_heads);
+  for (int i = threadIdx.x; i < 361 * HD; i += blockDim.x) {
+    int pos = i / HD, d = i - pos * HD;
+    int r = pbl_row(b, pos / 19, pos % 19);
+    Ks[i] = qkv[(size_t)r * ld + qc + kvh * HD + d];
+    Vs[i] = qkv[(size_t)r * ld + qc + kc + kvh * HD + d];
+  }
+  for (int pos = threadIdx.x; pos < 361; pos += blockDim.x) {
+    float m = rowmask[pbl_row(b, pos / 19, pos % 19)];
+    kb[pos] = m * 3e4f - 3e4f;
+  }
+  __syncthreads();
+  const int rr = blockIdx.x * 128 + threadIdx.x;
+  if (rr >= 400) return;
+  const int r = b * 400 + rr;
+  const int yy = rr / 20 - 1, xx = rr % 20;
+  T* o = out + (size_t)r * out_ld + h * HD;
+  if (yy < 0 || xx >= 19) {
+    for (int d = 0; d < HD; d++) o[d] = from_f<T>(0.0f);
+    return;
+  }
+  float q[HD], acc[HD];
+  for (int d = 0; d < HD; d++) {
+    q[d] = to_f<T>(qkv[(size_t)r * ld + h * HD + d]);
+    acc[d] = 0.0f;
+  }
+  float mx = -INFINITY, l = 0.0f;
+  for (int k = 0; k < 361; k++) {
+    float s = 0.0f;
+#pragma unroll
+    for (int d = 0; d < HD; d++) s += q[d] * to_f<T>(Ks[k * HD + d]);
+    s = s * scale + kb[k];
+    float mn = fmaxf(mx, s);
+    float corr = expf(mx - mn);
+    float pw = expf(s - mn);
+    l = l * corr + pw;
+#pragma unroll
+    for (int d = 0; d < HD; d++) acc[d] = acc[d] * corr + pw * to_f<T>(Vs[k * HD + d]);
+    mx = mn;
+  }
+  float inv = 1.0f / l;
+  for (int d = 0; d < HD; d++) o[d] = from_f<T>(acc[d] * inv);
+}
+
+}  // namespace kc

@@ -1,0 +1,38 @@
+"""Host-side symmetry helpers (the reference's SymmetryHelpers, crates/katago-core/src/neuralnet/nninputs.rs:756-899)
+exported by the library: a numpy restatement of getSymLoc semantics and the inverse property. CPU only."""
+
+import numpy as np
+import pytest
+
+from katago_cuda import api
+
+
+def sym_loc(x, y, size, s):
+    # nninputs.rs:909-924: flipX (bit 1), flipY (bit 0), then transpose (bit 2)
+    if s & 2:
+        x = size - x - 1
+    if s & 1:
+        y = size - y - 1
+    if s & 4:
+        x, y = y, x
+    return x, y
+
+
+@pytest.mark.parametrize("s", range(8))
+def test_inputs_follow_getsymloc(s):
+    rng = np.random.default_rng(s)
+    src = rng.standard_normal((1, 3, 19, 19)).astype(np.float32)
+    dst = api.copy_with_symmetry(src, 1, 19, 19, 3, s, False)
+    for y in range(19):
+        for x in range(19):
+            sx, sy = sym_loc(x, y, 19, s)
+            np.testing.assert_array_equal(dst[0, :, sy, sx], src[0, :, y, x])
+
+
+@pytest.mark.parametrize("s", range(8))
+def test_outputs_invert_inputs(s):
+    rng = np.random.default_rng(100 + s)
+    src = rng.standard_normal((1, 1, 19, 19)).astype(np.float32)
+    fwd = api.copy_with_symmetry(src, 1, 19, 19, 1, s, False)
+    back = api.copy_with_symmetry(fwd, 1, 19, 19, 1, s, True)
+    np.testing.assert_array_equal(back, src)
