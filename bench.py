@@ -232,6 +232,7 @@ def run_ours(args):
     stream.synchronize()
     torch.cuda.synchronize()
     clk = clocks.stop()
+    h.synchronize()
     if dist:
         dist.barrier()
     total_ms = sum(ev_s[i].elapsed_time(ev_e[i]) for i in range(args.steps))

@@ -7,6 +7,7 @@
 // fields by model version (:622-731).
 
 #include <chrono>
+#include <cstdlib>
 #include <cstring>
 #include <memory>
 #include <string>
@@ -335,6 +336,9 @@ int kc_handle_create(kc_context* ctx, int gpu_idx, int max_batch, int inputs_use
     KC_CUDA(cudaStreamCreateWithFlags(&h->stream, cudaStreamNonBlocking));
     KC_CUDA(cudaEventCreateWithFlags(&h->done, cudaEventDisableTiming));
     h->engine = std::make_unique<kc::Engine>(m, dev, max_batch, ctx->precision);
+    // KATAGO_CUDA_NO_GRAPHS=1 launches the forward kernel by kernel instead of through a CUDA graph (profilers)
+    const char* ng = std::getenv("KATAGO_CUDA_NO_GRAPHS");
+    if (ng && ng[0] == '1') h->engine->set_use_graphs(false);
     const int row_len = h->engine->layout().row_len;
     KC_CUDA(cudaMallocHost(&h->h_spatial, (size_t)max_batch * h->n_spatial * sizeof(float)));
     KC_CUDA(cudaMallocHost(&h->h_global, (size_t)max_batch * h->n_global * sizeof(float)));

@@ -393,7 +393,9 @@ struct Builder {
     const int K = p.taps * s.cin;
     Engine::Impl* Ip = &I;
     if constexpr (sizeof(T) == 2) {
-      int bn = pick_bn(s.N, s.mode == MODE_SWIGLU ? 32 : s.mode == MODE_ROPE ? s.head_dim : 16);
+      // SwiGLU splits each tile's linear1 half between two epilogue warps (BN % 64); RoPE gives each warp whole
+      // heads (BN % (2 * head_dim))
+      int bn = pick_bn(s.N, s.mode == MODE_SWIGLU ? 64 : s.mode == MODE_ROPE ? 2 * s.head_dim : 16);
       if (!bn) fail(KC_ERR_INVALID, "CUDA backend: no GEMM tile width for N = " + std::to_string(s.N));
       std::vector<float> Wp = s.W;
       if (s.mode == MODE_SWIGLU) {
@@ -652,7 +654,7 @@ struct Builder {
       dsin = up(sn);
     }
     const int tstride = b.use_rope && b.learnable_rope ? 361 * (hd / 2) : 0;
-    const bool fuse_rope = tc && b.use_rope && hd % 32 == 0;
+    const bool fuse_rope = tc && b.use_rope && hd % 32 == 0 && pick_bn(N, 2 * hd) != 0;
     if (fuse_rope) {
       s.mode = MODE_ROPE;
       Seg g;
@@ -737,7 +739,7 @@ struct Builder {
       pack_linear(s.W, s.cin, 0, b.w1);
       pack_linear(s.W, s.cin, F, b.wgate);
     }
-    const bool fuse = tc && F % 16 == 0 && pick_bn(2 * F, 32) != 0;
+    const bool fuse = tc && F % 16 == 0 && pick_bn(2 * F, 64) != 0;
     if (fuse) {
       s.mode = MODE_SWIGLU;
       Seg g;

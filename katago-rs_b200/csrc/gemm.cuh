@@ -105,15 +105,20 @@ template <> __device__ __forceinline__ __nv_bfloat16 from_f<__nv_bfloat16>(float
 
 // mish(x) = x * tanh(softplus(x)), with tanh(log(1 + e)) = (e^2 + 2e) / (e^2 + 2e + 2), e = exp(x), and the
 // identity above 20 (burn's softplus threshold, crates/katago-nn-burn/src/wino/kernels.rs:131).
+// silu(x) = x / (exp(-x) + 1) (bin2onnx.py:1163-1168), 0 below -80 where exp(-x) leaves the fast-divide range.
+// Both divide with __fdividef: the divisors stay below 2^126 on the branches taken.
 __device__ __forceinline__ float act_apply(float x, int act) {
   if (act == 1) return fmaxf(x, 0.0f);
   if (act == 2) {
-    if (x > 20.0f) return x;
-    float e = __expf(x);
+    float e = __expf(fminf(x, 20.0f));
     float n = e * (e + 2.0f);
-    return x * (n / (n + 2.0f));
+    float y = x * __fdividef(n, n + 2.0f);
+    return x > 20.0f ? x : y;
   }
-  if (act == 3) return x / (__expf(-x) + 1.0f);
+  if (act == 3) {
+    float y = __fdividef(x, __expf(-x) + 1.0f);
+    return x < -80.0f ? 0.0f : y;
+  }
   return x;
 }
 
@@ -180,18 +185,35 @@ __device__ __forceinline__ void store_zero(T* p) {
   for (int i = 0; i < CNT; i += PER) *reinterpret_cast<uint4*>(p + i) = make_uint4(0, 0, 0, 0);
 }
 
-// Segment epilogue for CNT consecutive columns [col0, col0 + CNT) of one row (all in one segment).
+__device__ __forceinline__ const EpiSeg& seg_of(const GemmParams& p, int col) {
+  if (p.nseg > 2 && col >= p.seg[1].n1) return p.seg[2];
+  if (p.nseg > 1 && col >= p.seg[0].n1) return p.seg[1];
+  return p.seg[0];
+}
+
+// The residual of CNT columns [c, c + CNT) of a segment (issued before the accumulator is read, to overlap).
 template <typename T, int CNT>
-__device__ __forceinline__ void epi_segment(const GemmParams& p, const RowInfo& ri, int col0, float (&v)[CNT]) {
+__device__ __forceinline__ void epi_load_res(const EpiSeg& s, const RowInfo& ri, int c, float (&rv)[CNT]) {
+  if ((s.flags & EPI_RESIDUAL) && ri.write) {
+    const size_t off = (size_t)ri.out_row * s.ld_res + s.res_c0 + c;
+    if (s.flags & EPI_RES_F32) load_vec<float, CNT>(reinterpret_cast<const float*>(s.res) + off, rv);
+    else load_vec<T, CNT>(reinterpret_cast<const T*>(s.res) + off, rv);
+  } else {
+#pragma unroll
+    for (int i = 0; i < CNT; i++) rv[i] = 0.0f;
+  }
+}
+
+// Segment epilogue for CNT consecutive columns [c, c + CNT) of segment s (c relative to the segment) of one row.
+// sc / bi: the BN scale and bias of those columns (shared or global memory).
+template <typename T, int CNT>
+__device__ __forceinline__ void epi_apply(const EpiSeg& s, const RowInfo& ri, int c, float (&v)[CNT],
+                                          const float (&rv)[CNT], const float* sc, const float* bi) {
   if (!ri.write) return;
-  const EpiSeg* s = &p.seg[0];
-  if (p.nseg > 1 && col0 >= p.seg[0].n1) s = &p.seg[1];
-  if (p.nseg > 2 && col0 >= p.seg[1].n1) s = &p.seg[2];
-  const int c = col0 - s->n0;
-  const int f = s->flags;
+  const int f = s.flags;
   const float m = ri.mask;
   if ((f & EPI_BOARD_BIAS) && m != 0.0f) {
-    const float* bb = s->board_bias + (size_t)ri.board * s->ld_bb + c;
+    const float* bb = s.board_bias + (size_t)ri.board * s.ld_bb + c;
 #pragma unroll
     for (int i = 0; i < CNT; i++) v[i] += __ldg(bb + i);
   }
@@ -200,10 +222,6 @@ __device__ __forceinline__ void epi_segment(const GemmParams& p, const RowInfo& 
     for (int i = 0; i < CNT; i++) v[i] *= m;
   }
   if (f & EPI_RESIDUAL) {
-    float rv[CNT];
-    const size_t off = (size_t)ri.out_row * s->ld_res + s->res_c0 + c;
-    if (f & EPI_RES_F32) load_vec<float, CNT>(reinterpret_cast<const float*>(s->res) + off, rv);
-    else load_vec<T, CNT>(reinterpret_cast<const T*>(s->res) + off, rv);
 #pragma unroll
     for (int i = 0; i < CNT; i++) v[i] += rv[i];
   }
@@ -211,24 +229,20 @@ __device__ __forceinline__ void epi_segment(const GemmParams& p, const RowInfo& 
     float o[CNT];
 #pragma unroll
     for (int i = 0; i < CNT; i++) o[i] = v[i] * m;
-    const size_t off = (size_t)ri.out_row * s->ld_raw + s->raw_c0 + c;
-    if (f & EPI_RAW_F32) store_vec<float, CNT>(reinterpret_cast<float*>(s->out_raw) + off, o);
-    else store_vec<T, CNT>(reinterpret_cast<T*>(s->out_raw) + off, o);
+    const size_t off = (size_t)ri.out_row * s.ld_raw + s.raw_c0 + c;
+    if (f & EPI_RAW_F32) store_vec<float, CNT>(reinterpret_cast<float*>(s.out_raw) + off, o);
+    else store_vec<T, CNT>(reinterpret_cast<T*>(s.out_raw) + off, o);
   }
   if (f & EPI_ACT) {
     float o[CNT];
-    if (m != 0.0f) {
+    const int act = s.act;
 #pragma unroll
-      for (int i = 0; i < CNT; i++) {
-        float t = v[i] * __ldg(s->scale + c + i);
-        t = t + __ldg(s->bias + c + i);
-        o[i] = act_apply(t, s->act) * m;
-      }
-    } else {
-#pragma unroll
-      for (int i = 0; i < CNT; i++) o[i] = 0.0f;
+    for (int i = 0; i < CNT; i++) {
+      float t = v[i] * sc[i];
+      t = t + bi[i];
+      o[i] = act_apply(t, act) * m;
     }
-    store_vec<T, CNT>(reinterpret_cast<T*>(s->out_act) + (size_t)ri.out_row * s->ld_act + s->act_c0 + c, o);
+    store_vec<T, CNT>(reinterpret_cast<T*>(s.out_act) + (size_t)ri.out_row * s.ld_act + s.act_c0 + c, o);
   }
 }
 
@@ -241,32 +255,47 @@ struct TcCfg {
   static constexpr int A_BYTES = 128 * 64 * 2;
   static constexpr int B_BYTES = BN * 64 * 2;
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
-  static constexpr int STAGES = (200 * 1024) / STAGE_BYTES > 8 ? 8 : (200 * 1024) / STAGE_BYTES;
+  static constexpr int PARAM_COLS = 768;  // per-column BN scale and bias staged in shared memory
+  static constexpr int PARAM_BYTES = PARAM_COLS * 2 * 4;
+  static constexpr int BAR_BYTES = 256;
+  static constexpr int SMEM_LIMIT = 227 * 1024;
+  static constexpr int FIT = (SMEM_LIMIT - 1024 - BAR_BYTES - PARAM_BYTES) / STAGE_BYTES;
+  static constexpr int STAGES = FIT > 8 ? 8 : FIT;
   static constexpr uint32_t ACC_COLS = BN <= 32 ? 32 : BN <= 64 ? 64 : BN <= 128 ? 128 : 256;
   static constexpr uint32_t TMEM_COLS = 2 * ACC_COLS;
-  static constexpr int BAR_BYTES = 256;
-  static constexpr int SMEM = 1024 /*align slack*/ + STAGES * STAGE_BYTES + BAR_BYTES;
-  static constexpr int THREADS = 192;
+  static constexpr int SMEM = 1024 /*align slack*/ + STAGES * STAGE_BYTES + BAR_BYTES + PARAM_BYTES;
+  static constexpr int EPI_WARPS = 8;  // two per TMEM lane quarter, splitting the tile's columns
+  static constexpr int THREADS = 64 + 32 * EPI_WARPS;
 };
 
+// Epilogue of one 128 x BN accumulator by the warp pair of one TMEM lane quarter; `half` selects this warp's
+// columns (interleaved 16-column chunks for segments, contiguous halves for SwiGLU and RoPE).
 template <typename T, int BN>
-__device__ __forceinline__ void tc_epilogue_tile(const GemmParams& p, uint32_t tacc, int m0, int n0, int row_in_tile) {
+__device__ __forceinline__ void tc_epilogue_tile(const GemmParams& p, const float* s_scale, const float* s_bias,
+                                                 uint32_t tacc, int m0, int n0, int row_in_tile, int half) {
   const RowInfo ri = row_info(p.g, m0 + row_in_tile);
   if (p.mode == MODE_SEGMENTS) {
 #pragma unroll 1
-    for (int c = 0; c < BN; c += 16) {
+    for (int c = half * 16; c < BN; c += 32) {
+      const int col = n0 + c;
+      const EpiSeg& s = seg_of(p, col);
+      float rv[16];
+      epi_load_res<T, 16>(s, ri, col - s.n0, rv);
       uint32_t u[16];
       tmem_ld16(tacc + c, u);
       tmem_wait_ld();
       float v[16];
 #pragma unroll
       for (int i = 0; i < 16; i++) v[i] = __uint_as_float(u[i]);
-      epi_segment<T, 16>(p, ri, n0 + c, v);
+      const bool tab = p.n_total <= TcCfg<BN>::PARAM_COLS;
+      const float* sc = tab ? s_scale + col : s.scale + (col - s.n0);
+      const float* bi = tab ? s_bias + col : s.bias + (col - s.n0);
+      epi_apply<T, 16>(s, ri, col - s.n0, v, rv, sc, bi);
     }
   } else if (p.mode == MODE_SWIGLU) {
     const EpiSeg& s = p.seg[0];
 #pragma unroll 1
-    for (int c = 0; c < BN / 2; c += 16) {
+    for (int c = half * (BN / 4); c < (half + 1) * (BN / 4); c += 16) {
       uint32_t ua[16], ug[16];
       tmem_ld16(tacc + c, ua);
       tmem_ld16(tacc + BN / 2 + c, ug);
@@ -276,30 +305,30 @@ __device__ __forceinline__ void tc_epilogue_tile(const GemmParams& p, uint32_t t
       for (int i = 0; i < 16; i++) {
         float a = __uint_as_float(ua[i]);
         float g = __uint_as_float(ug[i]);
-        h[i] = (a / (__expf(-a) + 1.0f)) * g * ri.mask;
+        h[i] = act_apply(a, 3) * g * ri.mask;
       }
       if (ri.write)
         store_vec<T, 16>(reinterpret_cast<T*>(s.out_raw) + (size_t)ri.out_row * s.ld_raw + n0 / 2 + c, h);
     }
   } else {  // MODE_ROPE: Q|K|V columns, Q and K heads rotated in halves of head_dim / 2
     const EpiSeg& s = p.seg[0];
-    const int hd = p.head_dim, half = hd / 2;
+    const int hd = p.head_dim, hh = hd / 2;
 #pragma unroll 1
-    for (int c = 0; c < BN; c += 16) {
+    for (int c = half * (BN / 2); c < (half + 1) * (BN / 2); c += 16) {
       const int gcol = n0 + c;
       if (gcol < p.rope_rot_cols) {
         const int within = gcol % hd;
-        if (within >= half) continue;  // written with its pair
+        if (within >= hh) continue;  // written with its pair
         uint32_t u0[16], u1[16];
         tmem_ld16(tacc + c, u0);
-        tmem_ld16(tacc + c + half, u1);
+        tmem_ld16(tacc + c + hh, u1);
         tmem_wait_ld();
         const int head = gcol / hd;
         int table;
         if (gcol < p.rope_q_cols) table = head / p.rope_group;
         else table = head - p.rope_q_cols / hd;
-        const float* ct = p.rope_cos + (size_t)table * p.rope_table_stride + (size_t)ri.pos * half + within;
-        const float* st = p.rope_sin + (size_t)table * p.rope_table_stride + (size_t)ri.pos * half + within;
+        const float* ct = p.rope_cos + (size_t)table * p.rope_table_stride + (size_t)ri.pos * hh + within;
+        const float* st = p.rope_sin + (size_t)table * p.rope_table_stride + (size_t)ri.pos * hh + within;
         float r0[16], r1[16];
 #pragma unroll
         for (int i = 0; i < 16; i++) {
@@ -311,7 +340,7 @@ __device__ __forceinline__ void tc_epilogue_tile(const GemmParams& p, uint32_t t
         if (ri.write) {
           T* o = reinterpret_cast<T*>(s.out_raw) + (size_t)ri.out_row * s.ld_raw + gcol;
           store_vec<T, 16>(o, r0);
-          store_vec<T, 16>(o + half, r1);
+          store_vec<T, 16>(o + hh, r1);
         }
       } else {
         uint32_t u[16];
@@ -327,7 +356,7 @@ __device__ __forceinline__ void tc_epilogue_tile(const GemmParams& p, uint32_t t
 }
 
 template <typename T, int BN>
-__global__ void __launch_bounds__(192, 1)
+__global__ void __launch_bounds__(TcCfg<BN>::THREADS, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                    const __grid_constant__ GemmParams p) {
   using C = TcCfg<BN>;
@@ -343,6 +372,18 @@ __global__ void __launch_bounds__(192, 1)
   uint64_t* drain = tempty + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  float* s_scale = reinterpret_cast<float*>(smem + C::STAGES * C::STAGE_BYTES + C::BAR_BYTES);
+  float* s_bias = s_scale + C::PARAM_COLS;
+
+  // per-column BN scale / bias of the act segments, staged once per CTA (zero where a segment has no BN)
+  if (p.n_total <= C::PARAM_COLS) {
+    for (int col = threadIdx.x; col < p.n_total; col += blockDim.x) {
+      const EpiSeg& s = seg_of(p, col);
+      const bool act = (s.flags & EPI_ACT) != 0;
+      s_scale[col] = act ? s.scale[col - s.n0] : 0.0f;
+      s_bias[col] = act ? s.bias[col - s.n0] : 0.0f;
+    }
+  }
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int m_tiles = (p.g.rows + 127) / 128;
@@ -358,7 +399,7 @@ __global__ void __launch_bounds__(192, 1)
     }
     for (int a = 0; a < 2; a++) {
       mbar_init(&tfull[a], 1);
-      mbar_init(&tempty[a], 128);
+      mbar_init(&tempty[a], 32 * C::EPI_WARPS);
     }
     mbar_init(drain, 1);
     *abort_flag = 0;
@@ -454,8 +495,9 @@ __global__ void __launch_bounds__(192, 1)
     }
     __syncwarp();
   } else {
-    // ---- epilogue warps 2..5: TMEM lane quarter = warp % 4 ----
+    // ---- epilogue warps 2..9: TMEM lane quarter = warp % 4, column half = (warp - 2) / 4 ----
     const int q = warp & 3;
+    const int half = (warp - 2) >> 2;
     const int row_in_tile = q * 32 + lane;
     int local = 0;
     for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, local++) {
@@ -470,7 +512,7 @@ __global__ void __launch_bounds__(192, 1)
       const int m0 = (tile / n_tiles) * 128;
       const int n0 = (tile % n_tiles) * BN;
       const uint32_t tacc = tmem_base + acc * C::ACC_COLS + ((uint32_t)(q * 32) << 16);
-      tc_epilogue_tile<T, BN>(p, tacc, m0, n0, row_in_tile);
+      tc_epilogue_tile<T, BN>(p, s_scale, s_bias, tacc, m0, n0, row_in_tile, half);
       tc_fence_before();
       mbar_arrive(&tempty[acc]);
     }
@@ -537,7 +579,11 @@ __global__ void __launch_bounds__(256) gemm_simt_kernel(const __grid_constant__ 
     const int r = m0 + ty * 4 + i;
     const RowInfo ri = row_info(p.g, r);
     float v[4] = {acc[i][0], acc[i][1], acc[i][2], acc[i][3]};
-    epi_segment<T, 4>(p, ri, ncol, v);
+    const EpiSeg& s = seg_of(p, ncol);
+    const int c = ncol - s.n0;
+    float rv[4];
+    epi_load_res<T, 4>(s, ri, c, rv);
+    epi_apply<T, 4>(s, ri, c, v, rv, s.scale + c, s.bias + c);
   }
 }
 
