@@ -372,6 +372,9 @@ struct Builder {
       e.act_c0 = g.act_c0;
     }
     if (s.mode == MODE_SEGMENTS && n0 != s.N) fail(KC_ERR_INVALID, "CUDA backend: GEMM segment widths != N");
+    for (int i = 0; i < p.nseg; i++)
+      if ((p.seg[i].flags & EPI_ACT) && s.N > TcCfg<256>::PARAM_COLS)
+        fail(KC_ERR_INVALID, "CUDA backend: batch-norm epilogue on a GEMM wider than 768 columns");
     p.rope_cos = s.rope_cos;
     p.rope_sin = s.rope_sin;
     p.rope_table_stride = s.rope_table_stride;

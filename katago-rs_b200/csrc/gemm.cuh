@@ -107,18 +107,29 @@ template <> __device__ __forceinline__ __nv_bfloat16 from_f<__nv_bfloat16>(float
 // identity above 20 (burn's softplus threshold, crates/katago-nn-burn/src/wino/kernels.rs:131).
 // silu(x) = x / (exp(-x) + 1) (bin2onnx.py:1163-1168), 0 below -80 where exp(-x) leaves the fast-divide range.
 // Both divide with __fdividef: the divisors stay below 2^126 on the branches taken.
-__device__ __forceinline__ float act_apply(float x, int act) {
-  if (act == 1) return fmaxf(x, 0.0f);
-  if (act == 2) {
+template <int ACT>
+__device__ __forceinline__ float act_fn(float x) {
+  if constexpr (ACT == 1) {
+    return fmaxf(x, 0.0f);
+  } else if constexpr (ACT == 2) {
     float e = __expf(fminf(x, 20.0f));
     float n = e * (e + 2.0f);
     float y = x * __fdividef(n, n + 2.0f);
     return x > 20.0f ? x : y;
-  }
-  if (act == 3) {
+  } else if constexpr (ACT == 3) {
     float y = __fdividef(x, __expf(-x) + 1.0f);
     return x < -80.0f ? 0.0f : y;
+  } else {
+    return x;
   }
+}
+
+// Runtime-selected activation, for the small kernels (per-element dispatch; the GEMM epilogue dispatches once per
+// 16-column unit on act_fn<ACT> instead).
+__device__ __forceinline__ float act_apply(float x, int act) {
+  if (act == 1) return act_fn<1>(x);
+  if (act == 2) return act_fn<2>(x);
+  if (act == 3) return act_fn<3>(x);
   return x;
 }
 
@@ -204,6 +215,18 @@ __device__ __forceinline__ void epi_load_res(const EpiSeg& s, const RowInfo& ri,
   }
 }
 
+// o = act(v * scale + bias) * mask (bin2onnx.py bn_act_mask :1170), the activation fixed at compile time.
+template <int CNT, int ACT>
+__device__ __forceinline__ void bn_act(const float (&v)[CNT], const float* sc, const float* bi, float m,
+                                       float (&o)[CNT]) {
+#pragma unroll
+  for (int i = 0; i < CNT; i++) {
+    float t = v[i] * sc[i];
+    t = t + bi[i];
+    o[i] = act_fn<ACT>(t) * m;
+  }
+}
+
 // Segment epilogue for CNT consecutive columns [c, c + CNT) of segment s (c relative to the segment) of one row.
 // sc / bi: the BN scale and bias of those columns (shared or global memory).
 template <typename T, int CNT>
@@ -235,12 +258,11 @@ __device__ __forceinline__ void epi_apply(const EpiSeg& s, const RowInfo& ri, in
   }
   if (f & EPI_ACT) {
     float o[CNT];
-    const int act = s.act;
-#pragma unroll
-    for (int i = 0; i < CNT; i++) {
-      float t = v[i] * sc[i];
-      t = t + bi[i];
-      o[i] = act_apply(t, act) * m;
+    switch (s.act) {
+      case 1: bn_act<CNT, 1>(v, sc, bi, m, o); break;
+      case 2: bn_act<CNT, 2>(v, sc, bi, m, o); break;
+      case 3: bn_act<CNT, 3>(v, sc, bi, m, o); break;
+      default: bn_act<CNT, 0>(v, sc, bi, m, o); break;
     }
     store_vec<T, CNT>(reinterpret_cast<T*>(s.out_act) + (size_t)ri.out_row * s.ld_act + s.act_c0 + c, o);
   }
@@ -275,22 +297,56 @@ __device__ __forceinline__ void tc_epilogue_tile(const GemmParams& p, const floa
                                                  uint32_t tacc, int m0, int n0, int row_in_tile, int half) {
   const RowInfo ri = row_info(p.g, m0 + row_in_tile);
   if (p.mode == MODE_SEGMENTS) {
+    // this warp's 16-column units are half, half + 2, half + 4, ...; two units per step share one TMEM wait, and
+    // the next step's residuals are loaded before this step's math so that their latency overlaps it
+    constexpr int UNITS = BN / 16;
+    float ra[16], rb[16];
+    {
+      const int ca = half * 16, cb = ca + 32;
+      const EpiSeg& sa = seg_of(p, n0 + ca);
+      epi_load_res<T, 16>(sa, ri, n0 + ca - sa.n0, ra);
+      if (cb < BN) {
+        const EpiSeg& sb = seg_of(p, n0 + cb);
+        epi_load_res<T, 16>(sb, ri, n0 + cb - sb.n0, rb);
+      }
+    }
 #pragma unroll 1
-    for (int c = half * 16; c < BN; c += 32) {
-      const int col = n0 + c;
-      const EpiSeg& s = seg_of(p, col);
-      float rv[16];
-      epi_load_res<T, 16>(s, ri, col - s.n0, rv);
-      uint32_t u[16];
-      tmem_ld16(tacc + c, u);
+    for (int u = half; u < UNITS; u += 4) {
+      const int ca = u * 16, cb = ca + 32;
+      const bool has_b = cb < BN;
+      uint32_t xa[16], xb[16];
+      tmem_ld16(tacc + ca, xa);
+      if (has_b) tmem_ld16(tacc + cb, xb);
+      float na[16], nb[16];
+      const int cn = ca + 64, cm = ca + 96;  // the next step's units
+      if (cn < BN) {
+        const EpiSeg& sn = seg_of(p, n0 + cn);
+        epi_load_res<T, 16>(sn, ri, n0 + cn - sn.n0, na);
+      }
+      if (cm < BN) {
+        const EpiSeg& sm = seg_of(p, n0 + cm);
+        epi_load_res<T, 16>(sm, ri, n0 + cm - sm.n0, nb);
+      }
       tmem_wait_ld();
-      float v[16];
+      {
+        const EpiSeg& s = seg_of(p, n0 + ca);
+        float v[16];
 #pragma unroll
-      for (int i = 0; i < 16; i++) v[i] = __uint_as_float(u[i]);
-      const bool tab = p.n_total <= TcCfg<BN>::PARAM_COLS;
-      const float* sc = tab ? s_scale + col : s.scale + (col - s.n0);
-      const float* bi = tab ? s_bias + col : s.bias + (col - s.n0);
-      epi_apply<T, 16>(s, ri, col - s.n0, v, rv, sc, bi);
+        for (int i = 0; i < 16; i++) v[i] = __uint_as_float(xa[i]);
+        epi_apply<T, 16>(s, ri, n0 + ca - s.n0, v, ra, s_scale + n0 + ca, s_bias + n0 + ca);
+      }
+      if (has_b) {
+        const EpiSeg& s = seg_of(p, n0 + cb);
+        float v[16];
+#pragma unroll
+        for (int i = 0; i < 16; i++) v[i] = __uint_as_float(xb[i]);
+        epi_apply<T, 16>(s, ri, n0 + cb - s.n0, v, rb, s_scale + n0 + cb, s_bias + n0 + cb);
+      }
+#pragma unroll
+      for (int i = 0; i < 16; i++) {
+        ra[i] = na[i];
+        rb[i] = nb[i];
+      }
     }
   } else if (p.mode == MODE_SWIGLU) {
     const EpiSeg& s = p.seg[0];
@@ -305,7 +361,7 @@ __device__ __forceinline__ void tc_epilogue_tile(const GemmParams& p, const floa
       for (int i = 0; i < 16; i++) {
         float a = __uint_as_float(ua[i]);
         float g = __uint_as_float(ug[i]);
-        h[i] = act_apply(a, 3) * g * ri.mask;
+        h[i] = act_fn<3>(a) * g * ri.mask;
       }
       if (ri.write)
         store_vec<T, 16>(reinterpret_cast<T*>(s.out_raw) + (size_t)ri.out_row * s.ld_raw + n0 / 2 + c, h);
@@ -375,8 +431,9 @@ __global__ void __launch_bounds__(TcCfg<BN>::THREADS, 1)
   float* s_scale = reinterpret_cast<float*>(smem + C::STAGES * C::STAGE_BYTES + C::BAR_BYTES);
   float* s_bias = s_scale + C::PARAM_COLS;
 
-  // per-column BN scale / bias of the act segments, staged once per CTA (zero where a segment has no BN)
-  if (p.n_total <= C::PARAM_COLS) {
+  // per-column BN scale / bias of the act segments, staged once per CTA (zero where a segment has no BN); the
+  // plan builder only gives segments with EPI_ACT to GEMMs of at most PARAM_COLS columns
+  if (p.mode == MODE_SEGMENTS && p.n_total <= C::PARAM_COLS) {
     for (int col = threadIdx.x; col < p.n_total; col += blockDim.x) {
       const EpiSeg& s = seg_of(p, col);
       const bool act = (s.flags & EPI_ACT) != 0;
