@@ -10,6 +10,7 @@
 
 #include <algorithm>
 #include <cmath>
+#include <cstdlib>
 #include <cstring>
 #include <functional>
 #include <map>
@@ -74,31 +75,56 @@ void allow_smem(K* kernel, int bytes) {
   done.insert(key);
 }
 
-template <typename T, int BN>
+template <typename T, int BN, bool RF32, bool WIN>
 void launch_tc_bn(bool prepare, int grid, cudaStream_t s, const CUtensorMap& a, const CUtensorMap& b,
                   const GemmParams& p) {
-  using C = TcCfg<BN>;
+  using C = TcCfg<BN, WIN>;
   if (prepare) {
-    allow_smem(gemm_tc_kernel<T, BN>, C::SMEM);
+    allow_smem(gemm_tc_kernel<T, BN, RF32, WIN>, C::SMEM);
     return;
   }
-  gemm_tc_kernel<T, BN><<<grid, C::THREADS, C::SMEM, s>>>(a, b, p);
+  gemm_tc_kernel<T, BN, RF32, WIN><<<grid, C::THREADS, C::SMEM, s>>>(a, b, p);
 }
 
-template <typename T>
-void launch_tc(bool prepare, int bn, int grid, cudaStream_t s, const CUtensorMap& a, const CUtensorMap& b,
-               const GemmParams& p) {
+template <typename T, bool RF32, bool WIN>
+void launch_tc_rf(bool prepare, int bn, int grid, cudaStream_t s, const CUtensorMap& a, const CUtensorMap& b,
+                  const GemmParams& p) {
   switch (bn) {
-    case 16: launch_tc_bn<T, 16>(prepare, grid, s, a, b, p); break;
-    case 32: launch_tc_bn<T, 32>(prepare, grid, s, a, b, p); break;
-    case 48: launch_tc_bn<T, 48>(prepare, grid, s, a, b, p); break;
-    case 64: launch_tc_bn<T, 64>(prepare, grid, s, a, b, p); break;
-    case 96: launch_tc_bn<T, 96>(prepare, grid, s, a, b, p); break;
-    case 128: launch_tc_bn<T, 128>(prepare, grid, s, a, b, p); break;
-    case 192: launch_tc_bn<T, 192>(prepare, grid, s, a, b, p); break;
-    case 256: launch_tc_bn<T, 256>(prepare, grid, s, a, b, p); break;
+    case 16: launch_tc_bn<T, 16, RF32, WIN>(prepare, grid, s, a, b, p); break;
+    case 32: launch_tc_bn<T, 32, RF32, WIN>(prepare, grid, s, a, b, p); break;
+    case 48: launch_tc_bn<T, 48, RF32, WIN>(prepare, grid, s, a, b, p); break;
+    case 64: launch_tc_bn<T, 64, RF32, WIN>(prepare, grid, s, a, b, p); break;
+    case 96: launch_tc_bn<T, 96, RF32, WIN>(prepare, grid, s, a, b, p); break;
+    case 128: launch_tc_bn<T, 128, RF32, WIN>(prepare, grid, s, a, b, p); break;
+    case 192: launch_tc_bn<T, 192, RF32, WIN>(prepare, grid, s, a, b, p); break;
+    case 256: launch_tc_bn<T, 256, RF32, WIN>(prepare, grid, s, a, b, p); break;
     default: fail(KC_ERR_INVALID, "CUDA backend: unsupported GEMM tile width " + std::to_string(bn));
   }
+}
+
+// rf32: the GEMM's residual is a float32 stream (only the bf16 tier has those); win: windowed multi-tap A loads
+template <typename T>
+void launch_tc(bool prepare, bool rf32, bool win, int bn, int grid, cudaStream_t s, const CUtensorMap& a,
+               const CUtensorMap& b, const GemmParams& p) {
+  if constexpr (std::is_same<T, __nv_bfloat16>::value) {
+    if (rf32) {
+      if (win) launch_tc_rf<T, true, true>(prepare, bn, grid, s, a, b, p);
+      else launch_tc_rf<T, true, false>(prepare, bn, grid, s, a, b, p);
+      return;
+    }
+  } else {
+    if (rf32) fail(KC_ERR_INVALID, "CUDA backend: float32 residual stream outside the bf16 tier");
+  }
+  if (win) launch_tc_rf<T, false, true>(prepare, bn, grid, s, a, b, p);
+  else launch_tc_rf<T, false, false>(prepare, bn, grid, s, a, b, p);
+}
+
+// How a windowed A start that is not a multiple of 8 rows is described to tcgen05. Measured on B200: the 128 B
+// swizzle follows the absolute shared-memory address bits, so the descriptor's base offset stays 0 (mode 1); the
+// row-phase base offset (mode 0) reads the wrong elements. KATAGO_CUDA_WIN_BASE overrides.
+int win_base_mode() {
+  const char* e = std::getenv("KATAGO_CUDA_WIN_BASE");
+  return e ? std::atoi(e) : 1;
 }
 
 // RoPE tables [tables][361][half] (desc.cpp computeRopeCosSin as restated in bin2onnx.py:449-484: float32 steps,
@@ -413,16 +439,31 @@ struct Builder {
       std::vector<T> Wt(Wp.size());
       for (size_t i = 0; i < Wp.size(); i++) Wt[i] = T(Wp[i]);
       T* dW = up(Wt);
-      CUtensorMap ta = make_map(s.A.p, bf16, s.A.ld, a_rows, 128);
+      // KATAGO_CUDA_WIN=1: multi-tap convolutions load one A window per 64-channel chunk (the tile plus its tap
+      // halo) shared by all taps. Off by default: it cuts L2 traffic by a third, but the misaligned window starts
+      // cost shared-memory bandwidth the M = 128 MMA already needs (3x3 192->192 at batch 256: 94 us vs 88 us).
+      const char* wenv = std::getenv("KATAGO_CUDA_WIN");
+      bool win = p.taps > 1 && wenv && wenv[0] == '1';
+      if (win) {
+        int halo = 0;
+        for (int i = 0; i < p.taps; i++) halo = std::max(halo, std::abs(p.tap_off[i]));
+        p.halo = halo;
+        p.win_rows = round_up(128 + 2 * halo, 8);
+        p.win_base_mode = win_base_mode();
+        if (p.win_rows > TcCfg<256, true>::WIN_MAX_ROWS) win = false;
+      }
+      CUtensorMap ta = make_map(s.A.p, bf16, s.A.ld, a_rows, win ? p.win_rows : 128);
       CUtensorMap tb = make_map(dW, bf16, K, s.N, bn);
       if (s.cin % 64 != 0) fail(KC_ERR_INVALID, "CUDA backend: GEMM input channels not padded");
-      launch_tc<T>(true, bn, 0, 0, ta, tb, p);
+      bool rf32 = false;
+      for (int i = 0; i < p.nseg; i++) rf32 = rf32 || (p.seg[i].flags & EPI_RES_F32);
+      launch_tc<T>(true, rf32, win, bn, 0, 0, ta, tb, p);
       add(s.cls, [=](cudaStream_t st, int n) {
         GemmParams q = p;
         q.g.rows = n * brows;
         int tiles = ((q.g.rows + 127) / 128) * (q.n_total / bn);
         int grid = std::min(tiles, Ip->sm_count);
-        launch_tc<T>(false, bn, grid, st, ta, tb, q);
+        launch_tc<T>(false, rf32, win, bn, grid, st, ta, tb, q);
       });
     } else {
       p.a = s.A.p;

@@ -86,6 +86,9 @@ struct GemmParams {
   int rope_table_stride = 0;        // floats between tables (0: one shared table)
   int rope_q_cols = 0, rope_rot_cols = 0, head_dim = 0, rope_group = 1;
   int* err = nullptr;
+  // windowed A (tensor-core kernel with WIN): one window of win_rows rows starting halo rows above the tile
+  int halo = 0, win_rows = 0;
+  int win_base_mode = 1;  // descriptor base offset of a shifted window start: 0 = its 128 B row phase, 1 = zero
   // SIMT kernel only
   const void* a = nullptr;
   int lda = 0;
@@ -272,80 +275,142 @@ __device__ __forceinline__ void epi_apply(const EpiSeg& s, const RowInfo& ri, in
 // tcgen05 persistent kernel
 // ================================================================================================================
 
-template <int BN>
+// Shared-memory plan of the tensor-core kernel. Without WIN a stage holds one A tile (128 rows x 64 channels) and
+// one B tile; with WIN (multi-tap convolutions) a ring of two A windows (up to 256 rows x 64 channels: the tile plus
+// its tap halo, loaded once per 64-channel chunk and shared by all taps) sits in front of B-only stages.
+template <int BN, bool WIN = false>
 struct TcCfg {
   static constexpr int A_BYTES = 128 * 64 * 2;
   static constexpr int B_BYTES = BN * 64 * 2;
-  static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+  static constexpr int WIN_MAX_ROWS = 256;
+  static constexpr int A_WIN_BYTES = WIN_MAX_ROWS * 128;
+  static constexpr int A_RING_BYTES = WIN ? 2 * A_WIN_BYTES : 0;
+  static constexpr int STAGE_BYTES = WIN ? B_BYTES : A_BYTES + B_BYTES;
   static constexpr int PARAM_COLS = 768;  // per-column BN scale and bias staged in shared memory
   static constexpr int PARAM_BYTES = PARAM_COLS * 2 * 4;
   static constexpr int BAR_BYTES = 256;
   static constexpr int SMEM_LIMIT = 227 * 1024;
-  static constexpr int FIT = (SMEM_LIMIT - 1024 - BAR_BYTES - PARAM_BYTES) / STAGE_BYTES;
+  static constexpr int FIT = (SMEM_LIMIT - 1024 - BAR_BYTES - PARAM_BYTES - A_RING_BYTES) / STAGE_BYTES;
   static constexpr int STAGES = FIT > 8 ? 8 : FIT;
   static constexpr uint32_t ACC_COLS = BN <= 32 ? 32 : BN <= 64 ? 64 : BN <= 128 ? 128 : 256;
   static constexpr uint32_t TMEM_COLS = 2 * ACC_COLS;
-  static constexpr int SMEM = 1024 /*align slack*/ + STAGES * STAGE_BYTES + BAR_BYTES + PARAM_BYTES;
+  static constexpr int SMEM = 1024 /*align slack*/ + A_RING_BYTES + STAGES * STAGE_BYTES + BAR_BYTES + PARAM_BYTES;
   static constexpr int EPI_WARPS = 8;  // two per TMEM lane quarter, splitting the tile's columns
   static constexpr int THREADS = 64 + 32 * EPI_WARPS;
 };
 
 // Epilogue of one 128 x BN accumulator by the warp pair of one TMEM lane quarter; `half` selects this warp's
 // columns (interleaved 16-column chunks for segments, contiguous halves for SwiGLU and RoPE).
-template <typename T, int BN>
+// Residual of one 16-column unit as raw 32-bit words (8 for 2-byte types, 16 for float32), loaded early.
+template <typename T, bool RF32>
+__device__ __forceinline__ void res_fetch(const EpiSeg& s, const RowInfo& ri, int c, uint32_t* w) {
+  constexpr int WORDS = RF32 ? 16 : 8;
+  if ((s.flags & EPI_RESIDUAL) && ri.write) {
+    const size_t off = (size_t)ri.out_row * s.ld_res + s.res_c0 + c;
+    const uint4* src = RF32 ? reinterpret_cast<const uint4*>(reinterpret_cast<const float*>(s.res) + off)
+                            : reinterpret_cast<const uint4*>(reinterpret_cast<const T*>(s.res) + off);
+#pragma unroll
+    for (int j = 0; j < WORDS / 4; j++) {
+      uint4 q = src[j];
+      w[4 * j] = q.x;
+      w[4 * j + 1] = q.y;
+      w[4 * j + 2] = q.z;
+      w[4 * j + 3] = q.w;
+    }
+  } else {
+#pragma unroll
+    for (int j = 0; j < WORDS; j++) w[j] = 0;
+  }
+}
+
+template <typename T, bool RF32>
+__device__ __forceinline__ void res_unpack(const uint32_t* w, float (&rv)[16]) {
+  if constexpr (RF32) {
+#pragma unroll
+    for (int i = 0; i < 16; i++) rv[i] = __uint_as_float(w[i]);
+  } else {
+    const T* e = reinterpret_cast<const T*>(w);
+#pragma unroll
+    for (int i = 0; i < 16; i++) rv[i] = to_f<T>(e[i]);
+  }
+}
+
+template <typename T, int BN, bool RF32>
 __device__ __forceinline__ void tc_epilogue_tile(const GemmParams& p, const float* s_scale, const float* s_bias,
                                                  uint32_t tacc, int m0, int n0, int row_in_tile, int half) {
   const RowInfo ri = row_info(p.g, m0 + row_in_tile);
   if (p.mode == MODE_SEGMENTS) {
-    // this warp's 16-column units are half, half + 2, half + 4, ...; two units per step share one TMEM wait, and
-    // the next step's residuals are loaded before this step's math so that their latency overlaps it
-    constexpr int UNITS = BN / 16;
-    float ra[16], rb[16];
-    {
-      const int ca = half * 16, cb = ca + 32;
-      const EpiSeg& sa = seg_of(p, n0 + ca);
-      epi_load_res<T, 16>(sa, ri, n0 + ca - sa.n0, ra);
-      if (cb < BN) {
-        const EpiSeg& sb = seg_of(p, n0 + cb);
-        epi_load_res<T, 16>(sb, ri, n0 + cb - sb.n0, rb);
-      }
-    }
+    // This warp's 16-column units are half, half + 2, half + 4, ... The residuals of a group of G units are all
+    // loaded before any of them is used (the whole tile for 2-byte residuals), so that one memory latency covers
+    // the group; then two units at a time share one TMEM wait.
+    constexpr int WORDS = RF32 ? 16 : 8;  // residual words per 16 columns
+    if constexpr (BN % 32 == 0) {
+      // 32-column blocks: block j goes to warp half j % 2; one 32-column TMEM load per block
+      constexpr int BLK = BN / 32;
+      constexpr int MY = (BLK + 1) / 2;
+      constexpr int G = RF32 ? (MY < 2 ? MY : 2) : MY;
 #pragma unroll 1
-    for (int u = half; u < UNITS; u += 4) {
-      const int ca = u * 16, cb = ca + 32;
-      const bool has_b = cb < BN;
-      uint32_t xa[16], xb[16];
-      tmem_ld16(tacc + ca, xa);
-      if (has_b) tmem_ld16(tacc + cb, xb);
-      float na[16], nb[16];
-      const int cn = ca + 64, cm = ca + 96;  // the next step's units
-      if (cn < BN) {
-        const EpiSeg& sn = seg_of(p, n0 + cn);
-        epi_load_res<T, 16>(sn, ri, n0 + cn - sn.n0, na);
-      }
-      if (cm < BN) {
-        const EpiSeg& sm = seg_of(p, n0 + cm);
-        epi_load_res<T, 16>(sm, ri, n0 + cm - sm.n0, nb);
-      }
-      tmem_wait_ld();
-      {
-        const EpiSeg& s = seg_of(p, n0 + ca);
-        float v[16];
+      for (int g0 = 0; g0 < MY; g0 += G) {
+        uint32_t rw[G][2 * WORDS];
 #pragma unroll
-        for (int i = 0; i < 16; i++) v[i] = __uint_as_float(xa[i]);
-        epi_apply<T, 16>(s, ri, n0 + ca - s.n0, v, ra, s_scale + n0 + ca, s_bias + n0 + ca);
-      }
-      if (has_b) {
-        const EpiSeg& s = seg_of(p, n0 + cb);
-        float v[16];
+        for (int k = 0; k < G; k++) {
+          const int b = half + 2 * (g0 + k);
+          if (b < BLK) {
 #pragma unroll
-        for (int i = 0; i < 16; i++) v[i] = __uint_as_float(xb[i]);
-        epi_apply<T, 16>(s, ri, n0 + cb - s.n0, v, rb, s_scale + n0 + cb, s_bias + n0 + cb);
-      }
+            for (int hh = 0; hh < 2; hh++) {
+              const int col = n0 + b * 32 + hh * 16;
+              const EpiSeg& s = seg_of(p, col);
+              res_fetch<T, RF32>(s, ri, col - s.n0, &rw[k][hh * WORDS]);
+            }
+          }
+        }
 #pragma unroll
-      for (int i = 0; i < 16; i++) {
-        ra[i] = na[i];
-        rb[i] = nb[i];
+        for (int k = 0; k < G; k++) {
+          const int b = half + 2 * (g0 + k);
+          if (b >= BLK) break;
+          uint32_t x[32];
+          tmem_ld32(tacc + b * 32, x);
+          tmem_wait_ld();
+#pragma unroll
+          for (int hh = 0; hh < 2; hh++) {
+            const int col = n0 + b * 32 + hh * 16;
+            const EpiSeg& s = seg_of(p, col);
+            float v[16], rv[16], sc[16], bi[16];
+#pragma unroll
+            for (int i = 0; i < 16; i++) v[i] = __uint_as_float(x[hh * 16 + i]);
+            res_unpack<T, RF32>(&rw[k][hh * WORDS], rv);
+            if (s.flags & EPI_ACT) {  // the tables only cover GEMMs with a BN segment (at most PARAM_COLS wide)
+              lds16(s_scale + col, sc);
+              lds16(s_bias + col, bi);
+            }
+            epi_apply<T, 16>(s, ri, col - s.n0, v, rv, sc, bi);
+          }
+        }
+      }
+    } else {
+      // 16-column units: unit u goes to warp half u % 2
+      constexpr int UNITS = BN / 16;
+      constexpr int MY = (UNITS + 1) / 2;
+#pragma unroll 1
+      for (int k = 0; k < MY; k++) {
+        const int u = half + 2 * k;
+        if (u >= UNITS) break;
+        const int col = n0 + u * 16;
+        const EpiSeg& s = seg_of(p, col);
+        uint32_t rw[WORDS];
+        res_fetch<T, RF32>(s, ri, col - s.n0, rw);
+        uint32_t x[16];
+        tmem_ld16(tacc + u * 16, x);
+        tmem_wait_ld();
+        float v[16], rv[16], sc[16], bi[16];
+#pragma unroll
+        for (int i = 0; i < 16; i++) v[i] = __uint_as_float(x[i]);
+        res_unpack<T, RF32>(rw, rv);
+        if (s.flags & EPI_ACT) {
+          lds16(s_scale + col, sc);
+          lds16(s_bias + col, bi);
+        }
+        epi_apply<T, 16>(s, ri, col - s.n0, v, rv, sc, bi);
       }
     }
   } else if (p.mode == MODE_SWIGLU) {
@@ -411,24 +476,29 @@ __device__ __forceinline__ void tc_epilogue_tile(const GemmParams& p, const floa
   }
 }
 
-template <typename T, int BN>
-__global__ void __launch_bounds__(TcCfg<BN>::THREADS, 1)
+// RF32: the residual segments read a float32 residual stream (the bf16 tier).
+// WIN: multi-tap convolution with one A window per 64-channel chunk shared by all taps (TcCfg).
+template <typename T, int BN, bool RF32, bool WIN>
+__global__ void __launch_bounds__(TcCfg<BN, WIN>::THREADS, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                    const __grid_constant__ GemmParams p) {
-  using C = TcCfg<BN>;
+  using C = TcCfg<BN, WIN>;
   constexpr int fmt = sizeof(T) == 2 && std::is_same<T, __nv_bfloat16>::value ? 1 : 0;
   constexpr uint32_t IDESC = make_idesc_f16(fmt, 128, BN);
 
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + C::STAGES * C::STAGE_BYTES);
+  uint8_t* stages = smem + C::A_RING_BYTES;  // WIN: the two A windows come first
+  uint64_t* full = reinterpret_cast<uint64_t*>(stages + C::STAGES * C::STAGE_BYTES);
   uint64_t* empty = full + C::STAGES;
   uint64_t* tfull = empty + C::STAGES;
   uint64_t* tempty = tfull + 2;
   uint64_t* drain = tempty + 2;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  uint64_t* afull = drain + 1;
+  uint64_t* aempty = afull + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(aempty + 2);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
-  float* s_scale = reinterpret_cast<float*>(smem + C::STAGES * C::STAGE_BYTES + C::BAR_BYTES);
+  float* s_scale = reinterpret_cast<float*>(stages + C::STAGES * C::STAGE_BYTES + C::BAR_BYTES);
   float* s_bias = s_scale + C::PARAM_COLS;
 
   // per-column BN scale / bias of the act segments, staged once per CTA (zero where a segment has no BN); the
@@ -457,6 +527,8 @@ __global__ void __launch_bounds__(TcCfg<BN>::THREADS, 1)
     for (int a = 0; a < 2; a++) {
       mbar_init(&tfull[a], 1);
       mbar_init(&tempty[a], 32 * C::EPI_WARPS);
+      mbar_init(&afull[a], 1);
+      mbar_init(&aempty[a], 1);
     }
     mbar_init(drain, 1);
     *abort_flag = 0;
@@ -479,24 +551,56 @@ __global__ void __launch_bounds__(TcCfg<BN>::THREADS, 1)
       int stage = 0;
       uint32_t phase = 0;
       bool ok = true;
+      int as = 0;
+      uint32_t aph = 0;
       for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
         const int m0 = (tile / n_tiles) * 128;
         const int n0 = (tile % n_tiles) * BN;
-        for (int kb = 0; kb < KB; kb++) {
-          if (!mbar_wait(&empty[stage], phase ^ 1, p.err, DEV_TIMEOUT_PRODUCER) || *abort_flag) {
-            ok = false;
-            *abort_flag = 1;
-            break;
+        if constexpr (WIN) {
+          // per 64-channel chunk: one A window (rows m0 - halo ...), then the chunk's B tile of every tap
+          for (int ch = 0; ch < kb_per_tap && ok; ch++) {
+            if (!mbar_wait(&aempty[as], aph ^ 1, p.err, DEV_TIMEOUT_PRODUCER) || *abort_flag) {
+              ok = false;
+              *abort_flag = 1;
+              break;
+            }
+            mbar_expect_tx(&afull[as], (uint32_t)p.win_rows * 128u);
+            tma_load_2d(smem + as * C::A_WIN_BYTES, &tmA, &afull[as], ch * 64, m0 - p.halo);
+            if (++as == 2) {
+              as = 0;
+              aph ^= 1;
+            }
+            for (int tap = 0; tap < p.taps; tap++) {
+              if (!mbar_wait(&empty[stage], phase ^ 1, p.err, DEV_TIMEOUT_PRODUCER) || *abort_flag) {
+                ok = false;
+                *abort_flag = 1;
+                break;
+              }
+              mbar_expect_tx(&full[stage], C::B_BYTES);
+              tma_load_2d(stages + stage * C::STAGE_BYTES, &tmB, &full[stage], tap * p.cin + ch * 64, n0);
+              if (++stage == C::STAGES) {
+                stage = 0;
+                phase ^= 1;
+              }
+            }
           }
-          const int tap = kb / kb_per_tap;
-          const int c0 = (kb - tap * kb_per_tap) * 64;
-          uint8_t* sa = smem + stage * C::STAGE_BYTES;
-          mbar_expect_tx(&full[stage], C::STAGE_BYTES);
-          tma_load_2d(sa, &tmA, &full[stage], c0, m0 + p.tap_off[tap]);
-          tma_load_2d(sa + C::A_BYTES, &tmB, &full[stage], kb * 64, n0);
-          if (++stage == C::STAGES) {
-            stage = 0;
-            phase ^= 1;
+        } else {
+          for (int kb = 0; kb < KB; kb++) {
+            if (!mbar_wait(&empty[stage], phase ^ 1, p.err, DEV_TIMEOUT_PRODUCER) || *abort_flag) {
+              ok = false;
+              *abort_flag = 1;
+              break;
+            }
+            const int tap = kb / kb_per_tap;
+            const int c0 = (kb - tap * kb_per_tap) * 64;
+            uint8_t* sa = stages + stage * C::STAGE_BYTES;
+            mbar_expect_tx(&full[stage], C::STAGE_BYTES);
+            tma_load_2d(sa, &tmA, &full[stage], c0, m0 + p.tap_off[tap]);
+            tma_load_2d(sa + C::A_BYTES, &tmB, &full[stage], kb * 64, n0);
+            if (++stage == C::STAGES) {
+              stage = 0;
+              phase ^= 1;
+            }
           }
         }
       }
@@ -513,6 +617,8 @@ __global__ void __launch_bounds__(TcCfg<BN>::THREADS, 1)
       // ---- MMA issuer ----
       int stage = 0;
       uint32_t phase = 0;
+      int as = 0;
+      uint32_t aph = 0;
       int local = 0;
       bool ok = true;
       for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x, local++) {
@@ -524,21 +630,58 @@ __global__ void __launch_bounds__(TcCfg<BN>::THREADS, 1)
         }
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + acc * C::ACC_COLS;
-        for (int kb = 0; kb < KB; kb++) {
-          if (!mbar_wait(&full[stage], phase, p.err, DEV_TIMEOUT_MMA) || *abort_flag) {
-            ok = false;
-            break;
-          }
-          tc_fence_after();
-          const uint32_t sa = smem_u32(smem + stage * C::STAGE_BYTES);
-          const uint32_t sb = sa + C::A_BYTES;
+        if constexpr (WIN) {
+          for (int ch = 0; ch < kb_per_tap && ok; ch++) {
+            if (!mbar_wait(&afull[as], aph, p.err, DEV_TIMEOUT_MMA) || *abort_flag) {
+              ok = false;
+              break;
+            }
+            const uint32_t swin = smem_u32(smem + as * C::A_WIN_BYTES);
+            for (int tap = 0; tap < p.taps; tap++) {
+              if (!mbar_wait(&full[stage], phase, p.err, DEV_TIMEOUT_MMA) || *abort_flag) {
+                ok = false;
+                break;
+              }
+              tc_fence_after();
+              // the tap's 128-row A tile starts halo + tap_off rows into the window
+              const int r0 = p.halo + p.tap_off[tap];
+              const uint32_t sa = swin + (uint32_t)r0 * 128u;
+              const uint32_t boff = p.win_base_mode == 0 ? (uint32_t)(r0 & 7) : 0u;
+              const uint32_t sb = smem_u32(stages + stage * C::STAGE_BYTES);
 #pragma unroll
-          for (int k = 0; k < 4; k++)
-            umma_f16(d_tmem, make_sw128_desc(sa + k * 32), make_sw128_desc(sb + k * 32), IDESC, (kb | k) != 0);
-          umma_commit(&empty[stage]);
-          if (++stage == C::STAGES) {
-            stage = 0;
-            phase ^= 1;
+              for (int k = 0; k < 4; k++)
+                umma_f16(d_tmem, make_sw128_desc(sa + k * 32, boff), make_sw128_desc(sb + k * 32), IDESC,
+                         (ch | tap | k) != 0);
+              umma_commit(&empty[stage]);
+              if (++stage == C::STAGES) {
+                stage = 0;
+                phase ^= 1;
+              }
+            }
+            if (!ok) break;
+            umma_commit(&aempty[as]);
+            if (++as == 2) {
+              as = 0;
+              aph ^= 1;
+            }
+          }
+        } else {
+          for (int kb = 0; kb < KB; kb++) {
+            if (!mbar_wait(&full[stage], phase, p.err, DEV_TIMEOUT_MMA) || *abort_flag) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+            const uint32_t sa = smem_u32(stages + stage * C::STAGE_BYTES);
+            const uint32_t sb = sa + C::A_BYTES;
+#pragma unroll
+            for (int k = 0; k < 4; k++)
+              umma_f16(d_tmem, make_sw128_desc(sa + k * 32), make_sw128_desc(sb + k * 32), IDESC, (kb | k) != 0);
+            umma_commit(&empty[stage]);
+            if (++stage == C::STAGES) {
+              stage = 0;
+              phase ^= 1;
+            }
           }
         }
         if (!ok) break;
@@ -569,7 +712,7 @@ __global__ void __launch_bounds__(TcCfg<BN>::THREADS, 1)
       const int m0 = (tile / n_tiles) * 128;
       const int n0 = (tile % n_tiles) * BN;
       const uint32_t tacc = tmem_base + acc * C::ACC_COLS + ((uint32_t)(q * 32) << 16);
-      tc_epilogue_tile<T, BN>(p, s_scale, s_bias, tacc, m0, n0, row_in_tile, half);
+      tc_epilogue_tile<T, BN, RF32>(p, s_scale, s_bias, tacc, m0, n0, row_in_tile, half);
       tc_fence_before();
       mbar_arrive(&tempty[acc]);
     }
