@@ -19,6 +19,7 @@
 #include <tuple>
 
 #include "common.h"
+#include "attention.cuh"
 #include "kernels.cuh"
 
 namespace kc {
@@ -732,6 +733,43 @@ struct Builder {
     }
     // attention
     const float scale = 1.0f / std::sqrt((float)hd);
+    if constexpr (sizeof(T) == 2) {
+      if (hd == 64) {
+        // tensor-core attention (attention.cuh): Q, K and V tiles straight from the QKV rows by TMA
+        if (pass == 1) {
+          const int qkv_rows = rows_for(QKV);
+          CUtensorMap tq = make_map(QKV.p, bf16, QKV.ld, qkv_rows, 128);
+          CUtensorMap tk = make_map(QKV.p, bf16, QKV.ld, qkv_rows, 208);
+          CUtensorMap tv = make_map(QKV.p, bf16, QKV.ld, qkv_rows, 224);
+          AttnParams ap;
+          ap.qc = qc;
+          ap.kc = kc;
+          ap.heads = nh;
+          ap.kv_heads = nkv;
+          ap.scale = scale;
+          ap.rowmask = I.rowmask;
+          ap.out = O.p;
+          ap.out_ld = O.ld;
+          ap.err = I.d_err;
+          allow_smem(attention_tc_kernel<T>, AttnCfg::SMEM);
+          add(CLS_ATTN, [=](cudaStream_t st, int n) {
+            attention_tc_kernel<T><<<dim3(4, nh, n), AttnCfg::THREADS, AttnCfg::SMEM, st>>>(tq, tk, tv, ap);
+          });
+        }
+        Spec so;
+        so.cls = CLS_LINEAR;
+        so.A = O;
+        so.cin = round_up(nh * vhd, 64);
+        so.N = w16(C);
+        if (pass == 1) {
+          so.W.assign((size_t)so.N * so.cin, 0.0f);
+          pack_linear(so.W, so.cin, 0, b.out);
+        }
+        so.segs = {close_seg(w16(C), X, XA, next, true)};
+        gemm(std::move(so));
+        return;
+      }
+    }
     if (pass == 1) {
       const int smem_need = 361 * hd * (int)sizeof(T) * 2 + 361 * (int)sizeof(float);
       if (hd == 16) allow_smem(attention_simt_kernel<T, 16>, smem_need);

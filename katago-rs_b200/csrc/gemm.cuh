@@ -71,7 +71,7 @@ struct GemmGeom {
   const float* rowmask = nullptr;  // [PBL rows]: 1 on board, 0 elsewhere
 };
 
-struct GemmParams {
+struct alignas(16) GemmParams {
   GemmGeom g;
   int n_total = 0;     // N (multiple of the tile width)
   int cin = 0;         // A channels per tap (multiple of 64 on the tensor-core path)
@@ -289,12 +289,15 @@ struct TcCfg {
   static constexpr int PARAM_COLS = 768;  // per-column BN scale and bias staged in shared memory
   static constexpr int PARAM_BYTES = PARAM_COLS * 2 * 4;
   static constexpr int BAR_BYTES = 256;
+  static constexpr int PCOPY_BYTES = 1024;  // a shared-memory copy of GemmParams
   static constexpr int SMEM_LIMIT = 227 * 1024;
-  static constexpr int FIT = (SMEM_LIMIT - 1024 - BAR_BYTES - PARAM_BYTES - A_RING_BYTES) / STAGE_BYTES;
+  static constexpr int FIT =
+      (SMEM_LIMIT - 1024 - BAR_BYTES - PARAM_BYTES - PCOPY_BYTES - A_RING_BYTES) / STAGE_BYTES;
   static constexpr int STAGES = FIT > 8 ? 8 : FIT;
   static constexpr uint32_t ACC_COLS = BN <= 32 ? 32 : BN <= 64 ? 64 : BN <= 128 ? 128 : 256;
   static constexpr uint32_t TMEM_COLS = 2 * ACC_COLS;
-  static constexpr int SMEM = 1024 /*align slack*/ + A_RING_BYTES + STAGES * STAGE_BYTES + BAR_BYTES + PARAM_BYTES;
+  static constexpr int SMEM =
+      1024 /*align slack*/ + A_RING_BYTES + STAGES * STAGE_BYTES + BAR_BYTES + PARAM_BYTES + PCOPY_BYTES;
   static constexpr int EPI_WARPS = 8;  // two per TMEM lane quarter, splitting the tile's columns
   static constexpr int THREADS = 64 + 32 * EPI_WARPS;
 };
@@ -335,10 +338,23 @@ __device__ __forceinline__ void res_unpack(const uint32_t* w, float (&rv)[16]) {
   }
 }
 
-template <typename T, int BN, bool RF32>
-__device__ __forceinline__ void tc_epilogue_tile(const GemmParams& p, const float* s_scale, const float* s_bias,
-                                                 uint32_t tacc, int m0, int n0, int row_in_tile, int half) {
-  const RowInfo ri = row_info(p.g, m0 + row_in_tile);
+// The segment of a column: with SINGLE (one-segment GEMMs, the trunk's convolutions and linears) always the
+// register-resident copy s0, so the per-unit epilogue code reads no descriptor memory at all.
+template <bool SINGLE>
+struct SegPick {
+  const GemmParams& p;
+  const EpiSeg& s0;
+  __device__ __forceinline__ const EpiSeg& operator()(int col) const {
+    if constexpr (SINGLE) return s0;
+    else return seg_of(p, col);
+  }
+};
+
+template <typename T, int BN, bool RF32, bool SINGLE>
+__device__ __forceinline__ void tc_epilogue_tile(const GemmParams& p, const EpiSeg& s0, const RowInfo& ri,
+                                                 const float* s_scale, const float* s_bias, uint32_t tacc, int n0,
+                                                 int half) {
+  const SegPick<SINGLE> pick{p, s0};
   if (p.mode == MODE_SEGMENTS) {
     // This warp's 16-column units are half, half + 2, half + 4, ... The residuals of a group of G units are all
     // loaded before any of them is used (the whole tile for 2-byte residuals), so that one memory latency covers
@@ -359,7 +375,7 @@ __device__ __forceinline__ void tc_epilogue_tile(const GemmParams& p, const floa
 #pragma unroll
             for (int hh = 0; hh < 2; hh++) {
               const int col = n0 + b * 32 + hh * 16;
-              const EpiSeg& s = seg_of(p, col);
+              const EpiSeg& s = pick(col);
               res_fetch<T, RF32>(s, ri, col - s.n0, &rw[k][hh * WORDS]);
             }
           }
@@ -374,7 +390,7 @@ __device__ __forceinline__ void tc_epilogue_tile(const GemmParams& p, const floa
 #pragma unroll
           for (int hh = 0; hh < 2; hh++) {
             const int col = n0 + b * 32 + hh * 16;
-            const EpiSeg& s = seg_of(p, col);
+            const EpiSeg& s = pick(col);
             float v[16], rv[16], sc[16], bi[16];
 #pragma unroll
             for (int i = 0; i < 16; i++) v[i] = __uint_as_float(x[hh * 16 + i]);
@@ -396,7 +412,7 @@ __device__ __forceinline__ void tc_epilogue_tile(const GemmParams& p, const floa
         const int u = half + 2 * k;
         if (u >= UNITS) break;
         const int col = n0 + u * 16;
-        const EpiSeg& s = seg_of(p, col);
+        const EpiSeg& s = pick(col);
         uint32_t rw[WORDS];
         res_fetch<T, RF32>(s, ri, col - s.n0, rw);
         uint32_t x[16];
@@ -500,6 +516,13 @@ __global__ void __launch_bounds__(TcCfg<BN, WIN>::THREADS, 1)
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   float* s_scale = reinterpret_cast<float*>(stages + C::STAGES * C::STAGE_BYTES + C::BAR_BYTES);
   float* s_bias = s_scale + C::PARAM_COLS;
+  GemmParams* s_params = reinterpret_cast<GemmParams*>(s_bias + C::PARAM_COLS);
+
+  // The roles read the parameters from a shared-memory copy: fields of the __grid_constant__ struct reached through
+  // references with run-time indices (segment lookups per 16 columns) cost hundreds of cycles each.
+  static_assert(sizeof(GemmParams) <= C::PCOPY_BYTES && sizeof(GemmParams) % 16 == 0, "parameter copy");
+  for (int i = threadIdx.x; i < (int)(sizeof(GemmParams) / 16); i += blockDim.x)
+    reinterpret_cast<uint4*>(s_params)[i] = reinterpret_cast<const uint4*>(&p)[i];
 
   // per-column BN scale / bias of the act segments, staged once per CTA (zero where a segment has no BN); the
   // plan builder only gives segments with EPI_ACT to GEMMs of at most PARAM_COLS columns
@@ -595,7 +618,7 @@ __global__ void __launch_bounds__(TcCfg<BN, WIN>::THREADS, 1)
             const int c0 = (kb - tap * kb_per_tap) * 64;
             uint8_t* sa = stages + stage * C::STAGE_BYTES;
             mbar_expect_tx(&full[stage], C::STAGE_BYTES);
-            tma_load_2d(sa, &tmA, &full[stage], c0, m0 + p.tap_off[tap]);
+            tma_load_2d(sa, &tmA, &full[stage], c0, m0 + s_params->tap_off[tap]);
             tma_load_2d(sa + C::A_BYTES, &tmB, &full[stage], kb * 64, n0);
             if (++stage == C::STAGES) {
               stage = 0;
@@ -644,7 +667,7 @@ __global__ void __launch_bounds__(TcCfg<BN, WIN>::THREADS, 1)
               }
               tc_fence_after();
               // the tap's 128-row A tile starts halo + tap_off rows into the window
-              const int r0 = p.halo + p.tap_off[tap];
+              const int r0 = p.halo + s_params->tap_off[tap];
               const uint32_t sa = swin + (uint32_t)r0 * 128u;
               const uint32_t boff = p.win_base_mode == 0 ? (uint32_t)(r0 & 7) : 0u;
               const uint32_t sb = smem_u32(stages + stage * C::STAGE_BYTES);
@@ -699,20 +722,22 @@ __global__ void __launch_bounds__(TcCfg<BN, WIN>::THREADS, 1)
     const int q = warp & 3;
     const int half = (warp - 2) >> 2;
     const int row_in_tile = q * 32 + lane;
+    const GemmParams& sp = *s_params;
     int local = 0;
     for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, local++) {
       const int acc = local & 1;
       const uint32_t acc_phase = (local >> 1) & 1;
+      const int m0 = (tile / n_tiles) * 128;
+      const int n0 = (tile % n_tiles) * BN;
+      const RowInfo ri = row_info(sp.g, m0 + row_in_tile);  // its mask load overlaps the wait
       if (!mbar_wait(&tfull[acc], acc_phase, p.err, DEV_TIMEOUT_EPILOGUE) || *abort_flag) {
         *abort_flag = 1;
         break;
       }
       __syncwarp();
       tc_fence_after();
-      const int m0 = (tile / n_tiles) * 128;
-      const int n0 = (tile % n_tiles) * BN;
       const uint32_t tacc = tmem_base + acc * C::ACC_COLS + ((uint32_t)(q * 32) << 16);
-      tc_epilogue_tile<T, BN, RF32>(p, s_scale, s_bias, tacc, m0, n0, row_in_tile, half);
+      tc_epilogue_tile<T, BN, RF32, false>(sp, sp.seg[0], ri, s_scale, s_bias, tacc, n0, half);
       tc_fence_before();
       mbar_arrive(&tempty[acc]);
     }

@@ -48,6 +48,17 @@ __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
 
 __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   uint32_t ok;
+#ifdef KC_MBAR_TEST_WAIT
+  asm volatile(
+      "{\n"
+      " .reg .pred p;\n"
+      " mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n"
+      " selp.u32 %0, 1, 0, p;\n"
+      "}\n"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+#else
   asm volatile(
       "{\n"
       " .reg .pred p;\n"
@@ -57,17 +68,23 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
       : "=r"(ok)
       : "r"(smem_u32(bar)), "r"(parity)
       : "memory");
+#endif
   return ok != 0;
 }
 
+// Every spin-wait gives up after this many SM clock cycles (about 2 s at the B200's clocks).
+constexpr long long kWaitLimitCycles = 4000ll * 1000ll * 1000ll;
+
 // Wait for the phase with `parity` to complete; false (and the error word set) if it did not within the limit.
+// The limit is checked on the SM's own cycle counter, and only every 256 polls: reading the global timer on every
+// miss put microseconds of latency on each pipeline hand-off.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* err, int code) {
   if (mbar_try_wait(bar, parity)) return true;
-  unsigned long long t0 = globaltimer();
+  const long long t0 = clock64();
   while (true) {
-    for (int i = 0; i < 32; i++)
+    for (int i = 0; i < 256; i++)
       if (mbar_try_wait(bar, parity)) return true;
-    if (globaltimer() - t0 > kWaitLimitNs) {
+    if (clock64() - t0 > kWaitLimitCycles) {
       if (err) atomicCAS(err, 0, code);
       return false;
     }
@@ -121,7 +138,9 @@ __device__ __forceinline__ void umma_commit(uint64_t* bar) {
 }
 
 // 32 TMEM lanes x 16 consecutive 32-bit columns: thread i of the warp gets lane (base lane + i).
+// tcgen05.ld is .sync.aligned: the warp is reconverged first (callers branch per lane before it).
 __device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
+  __syncwarp();
   asm volatile(
       "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
       : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
@@ -129,10 +148,14 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
       : "r"(taddr)
       : "memory");
 }
-__device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+__device__ __forceinline__ void tmem_wait_ld() {
+  __syncwarp();
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
 
 // 32 TMEM lanes x 32 consecutive 32-bit columns.
 __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
+  __syncwarp();
   asm volatile(
       "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18,%19,"
       "%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
