@@ -153,6 +153,15 @@ int kc_handle_profile(kc_handle* h, double* ms_by_class, int64_t* launches_by_cl
 int kc_handle_launch_count(kc_handle* h, int n, int* launches);
 int kc_model_flops(const kc_model* model, double* flops_per_row, double* conv3x3_flops_per_row);
 
+/* KataGo's masked global pooling followed by the gpool-to-bias matmul, on device tensors in the reference layout:
+ * x [n][c][19*19] float32 (already masked), mask [n][19*19] (input channel 0), w [3c][oc], out [n][oc]:
+ *   out[b] = [mean, mean * (sqrt(area) - 14) / 10, max over on-board points] x w
+ * (tools/bin2onnx/bin2onnx.py gpool :1222-1230 and the matmul after it, :1255 / :1501). Enqueued on `stream`
+ * (a cudaStream_t, NULL = legacy default stream); the pooled [n][3c] scratch is taken from the stream-ordered
+ * allocator (cudaMallocAsync) and released after use. 3c <= 12288. */
+int kc_gpool_fc(const float* d_x, const float* d_mask, int n, int c, const float* d_w, int oc, float* d_out,
+                void* stream);
+
 /* Host-side symmetry helpers of the reference (nninputs.rs:756-879), exported for tests of the host logic.
  * NCHW copy of one row with `c_size` channels; `reverse` = copyOutputsWithSymmetry semantics. */
 int kc_copy_with_symmetry(const float* src, float* dst, int n_size, int h_size, int w_size, int c_size,

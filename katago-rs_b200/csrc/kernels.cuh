@@ -50,7 +50,7 @@ struct BoardParams {
   float* scale2;         // [n]
 };
 
-__global__ void board_kernel(const __grid_constant__ BoardParams p) {
+static __global__ void board_kernel(const __grid_constant__ BoardParams p) {
   __shared__ float red[256];
   __shared__ float hbuf[2][512];
   const int b = blockIdx.x;
@@ -143,7 +143,7 @@ __global__ void pool_kernel(const T* __restrict__ x, int ld, int c0, int C, cons
 // Small per-board matmul: out[b][off + o * ostride] = act(sum_i in[b][i] * W[i][o] (+ bias[o])).
 // grid n, block 128.
 // ---------------------------------------------------------------------------------------------------------------
-__global__ void fc_kernel(const float* __restrict__ in, int in_ld, int ic, const float* __restrict__ w, int oc,
+static __global__ void fc_kernel(const float* __restrict__ in, int in_ld, int ic, const float* __restrict__ w, int oc,
                           const float* __restrict__ bias, int act, float* __restrict__ out, int out_ld, int out_off,
                           int out_stride) {
   extern __shared__ float xin[];

@@ -1,0 +1,94 @@
+// Standalone operator entry points of the katago-rs B200 backend (C ABI): KataGo's masked global pooling followed
+// by the gpool-to-bias matmul, on reference-layout (NCHW float32) device tensors. This is the computation of a
+// gpool block's bias branch and of the policy head's g1 branch (tools/bin2onnx/bin2onnx.py gpool :1222-1230 and
+// the matmul that follows it at :1255 and :1501), for callers that run it outside a whole forward pass.
+
+#include <cuda_runtime.h>
+
+#include <string>
+
+#include "../../include/katago_cuda.h"
+#include "common.h"
+#include "kernels.cuh"
+
+namespace kc {
+
+// pooled[b][c], [C + c], [2C + c] = mean, mean * (sqrt(area) - 14) / 10, max(x + (mask * 1e4 - 1e4)) over the
+// board's 361 points of channel c (x already masked). One warp per (board, channel); block (32, 8).
+__global__ void gpool_nchw_kernel(const float* __restrict__ x, const float* __restrict__ mask, int n, int C,
+                                  float* __restrict__ pooled) {
+  const int b = blockIdx.x;
+  const int c = blockIdx.y * 8 + threadIdx.y;
+  if (c >= C) return;
+  const float* xr = x + ((size_t)b * C + c) * 361;
+  const float* mr = mask + (size_t)b * 361;
+  float s = 0.0f, ms = 0.0f, mx = -INFINITY;
+  for (int i = threadIdx.x; i < 361; i += 32) {
+    const float v = xr[i], m = mr[i];
+    s += v;
+    ms += m;
+    const float biasv = m * 1e4f - 1e4f;
+    mx = fmaxf(mx, v + biasv);
+  }
+  for (int o = 16; o > 0; o >>= 1) {
+    s += __shfl_xor_sync(0xffffffffu, s, o);
+    ms += __shfl_xor_sync(0xffffffffu, ms, o);
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+  }
+  if (threadIdx.x == 0) {
+    const float mean = s / ms;
+    const float cen = sqrtf(ms) - 14.0f;
+    float* o = pooled + (size_t)b * 3 * C;
+    o[c] = mean;
+    o[C + c] = mean * (cen * 0.1f);
+    o[2 * C + c] = mx;
+  }
+}
+
+void check_gpool_args(const float* x, const float* mask, int n, int c, const float* w, int oc, const float* out) {
+  if (!x || !mask || !w || !out) fail(KC_ERR_INVALID, "CUDA backend: gpool: null tensor");
+  if (n < 1 || c < 1 || oc < 1) fail(KC_ERR_INVALID, "CUDA backend: gpool: sizes must be positive");
+  if (3 * c > 12 * 1024) fail(KC_ERR_INVALID, "CUDA backend: gpool: 3 * channels above 12288");
+}
+
+// pooled (scratch [n][3c]) -> out = pooled x w ([3c][oc]), both launched on `st`.
+void launch_gpool_fc(const float* x, const float* mask, int n, int c, const float* w, int oc, float* out,
+                     float* pooled, cudaStream_t st) {
+  gpool_nchw_kernel<<<dim3(n, (c + 7) / 8), dim3(32, 8), 0, st>>>(x, mask, n, c, pooled);
+  KC_CUDA(cudaGetLastError());
+  fc_kernel<<<n, 128, 3 * c * sizeof(float), st>>>(pooled, 3 * c, 3 * c, w, oc, nullptr, 0, out, oc, 0, 1);
+  KC_CUDA(cudaGetLastError());
+}
+
+}  // namespace kc
+
+namespace {
+template <typename F>
+int guard_op(F&& f) {
+  try {
+    f();
+    kc::set_last_error("");
+    return KC_OK;
+  } catch (const kc::Error& e) {
+    kc::set_last_error(e.what());
+    return e.status;
+  }
+}
+}  // namespace
+
+extern "C" int kc_gpool_fc(const float* d_x, const float* d_mask, int n, int c, const float* d_w, int oc,
+                           float* d_out, void* stream) {
+  return guard_op([&] {
+    kc::check_gpool_args(d_x, d_mask, n, c, d_w, oc, d_out);
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    float* pooled = nullptr;
+    KC_CUDA(cudaMallocAsync(reinterpret_cast<void**>(&pooled), (size_t)n * 3 * c * sizeof(float), st));
+    try {
+      kc::launch_gpool_fc(d_x, d_mask, n, c, d_w, oc, d_out, pooled, st);
+    } catch (...) {
+      cudaFreeAsync(pooled, st);
+      throw;
+    }
+    KC_CUDA(cudaFreeAsync(pooled, st));
+  });
+}

@@ -88,6 +88,7 @@ _SIGS = {
     "kc_handle_profile": ([P, ctypes.POINTER(ctypes.c_double), ctypes.POINTER(ctypes.c_int64), I], I),
     "kc_handle_launch_count": ([P, I, ctypes.POINTER(I)], I),
     "kc_copy_with_symmetry": ([FP, FP, I, I, I, I, I, I], I),
+    "kc_gpool_fc": ([P, P, I, I, P, I, P, P], I),
 }
 
 
@@ -281,6 +282,11 @@ class Handle:
         c = I()
         _check(lib().kc_handle_launch_count(self.h, n, ctypes.byref(c)))
         return c.value
+
+
+def gpool_fc(d_x: int, d_mask: int, n: int, c: int, d_w: int, oc: int, d_out: int, stream: int = 0):
+    """kc_gpool_fc on device pointers (masked global pooling + gpool-to-bias matmul)."""
+    _check(lib().kc_gpool_fc(d_x, d_mask, n, c, d_w, oc, d_out, stream or None))
 
 
 def copy_with_symmetry(src: np.ndarray, n: int, h: int, w: int, c: int, symmetry: int, reverse: bool) -> np.ndarray:
