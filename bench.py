@@ -32,6 +32,9 @@ sys.path.insert(0, os.path.join(REPO, "katago-rs_b200", "python"))
 
 METRIC = "b18c384nbt evals/s at batch 256 per GPU"
 UNIT = "evals/s"
+# DRAM bytes (read + write) per 3x3-convolution GEMM launch at batch 256, from the full ncu capture summarised in
+# profiles/gemm_tc_b18c384nbt_batch256.md (mean of the two 3x3 launches captured).
+CONV3_DRAM_BYTES_PER_LAUNCH = 73.6e6
 
 
 def parse():
@@ -53,6 +56,19 @@ def dist_env():
     world = int(os.environ.get("WORLD_SIZE", "1"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
     return rank, world, local
+
+
+def reduce_timing(total_ms, rows_per_rank, steps, dist=None, device=None):
+    """(value, max_ms): the timed region's device time as the max over ranks, and all ranks' rows / that time
+    (every rank runs the same per-GPU batch: weak scaling)."""
+    import torch
+    t = torch.tensor([float(total_ms)], dtype=torch.float64, device=device)
+    world = 1
+    if dist is not None and dist.is_initialized():
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        world = dist.get_world_size()
+    max_ms = float(t.item())
+    return world * rows_per_rank * steps / (max_ms / 1e3), max_ms
 
 
 def workload(args, rank):
@@ -249,11 +265,7 @@ def run_ours(args):
     clk = clocks.stop()
     if dist:
         dist.barrier()
-    t = torch.tensor([total_ms], dtype=torch.float64, device=dev)
-    if dist:
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    max_ms = float(t.item())
-    value = world * args.batch * args.steps / (max_ms / 1e3)
+    value, max_ms = reduce_timing(total_ms, args.batch, args.steps, dist, dev)
 
     # parity spot check of this run's output rows (no oracle: finite values only)
     out = d_out.cpu().numpy()
@@ -279,10 +291,7 @@ def run_ours(args):
         h.wait()
     torch.cuda.synchronize()
     e2e_ms = sum(e_s[i].elapsed_time(e_e[i]) for i in range(args.steps))
-    t = torch.tensor([e2e_ms], dtype=torch.float64, device=dev)
-    if dist:
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    e2e_value = world * args.batch * args.steps / (float(t.item()) / 1e3)
+    e2e_value, _ = reduce_timing(e2e_ms, args.batch, args.steps, dist, dev)
 
     if rank == 0:
         burst, sustained, hbm, src = peaks()
@@ -305,7 +314,9 @@ def run_ours(args):
                        "parallelism": f"replicas x{world} (no collective)",
                        "l2": "flushed between timed steps (256 MiB write, outside the timed events)"},
             "roofline": {"bound": "tensor", "achieved": achieved, "peak": sustained, "unit": "TFLOP/s", "frac": frac,
-                         "traffic": None, "kernel": "gemm_tc_kernel (3x3 conv implicit GEMM)",
+                         "traffic": CONV3_DRAM_BYTES_PER_LAUNCH if args.net == "b18c384nbt" and args.batch == 256
+                         else None,
+                         "kernel": "gemm_tc_kernel (3x3 conv implicit GEMM)",
                          "peak_kind": f"{src} bf16 sustained"},
             "kernels": other,
             "profiled_ms_per_step": prof_ms / args.steps,
