@@ -162,6 +162,21 @@ int kc_model_flops(const kc_model* model, double* flops_per_row, double* conv3x3
 int kc_gpool_fc(const float* d_x, const float* d_mask, int n, int c, const float* d_w, int oc, float* d_out,
                 void* stream);
 
+/* kc_gpool_fc for callers that cannot allocate GPU memory — for instance a host that reserves the device memory up
+ * front for its own pools and forbids later allocations, or a latency-critical thread that cannot afford
+ * cudaMalloc's device-wide synchronisation. This entry point has no counterpart in the reference; it allocates
+ * nothing (no cudaMalloc, cudaFree or allocating library call). Its pooled [n][3c] scratch is one fixed array of
+ * KC_GPOOL_NOALLOC_MAX_FLOATS floats (1 MiB) in device memory, present on every GPU that loads this library until
+ * the process exits; larger n * 3c is rejected with KC_ERR_INVALID. The first call on a device looks up that
+ * array's device address (once per device, with that device current), so make the first call on each device
+ * before any stream capture. All calls share the one array and it keeps the last call's contents (every entry a
+ * call reads is written by that call first): calls whose work overlaps on the GPU (different streams, or
+ * different host threads on one device) race on it and must be ordered by the caller. Inputs, outputs and
+ * stream are as for kc_gpool_fc. */
+#define KC_GPOOL_NOALLOC_MAX_FLOATS 262144
+int kc_gpool_fc_noalloc(const float* d_x, const float* d_mask, int n, int c, const float* d_w, int oc, float* d_out,
+                        void* stream);
+
 /* Host-side symmetry helpers of the reference (nninputs.rs:756-879), exported for tests of the host logic.
  * NCHW copy of one row with `c_size` channels; `reverse` = copyOutputsWithSymmetry semantics. */
 int kc_copy_with_symmetry(const float* src, float* dst, int n_size, int h_size, int w_size, int c_size,

@@ -5,6 +5,7 @@
 
 #include <cuda_runtime.h>
 
+#include <mutex>
 #include <string>
 
 #include "../../include/katago_cuda.h"
@@ -75,6 +76,46 @@ int guard_op(F&& f) {
   }
 }
 }  // namespace
+
+// ---------------------------------------------------------------------------------------------------------------
+// Allocation-free variant. Its scratch (the pooled [n][3c] vector) is this fixed device array, present on every
+// GPU that loads the library for as long as the process lives. Host code must not pass the symbol itself to a
+// kernel: on the host, g_gpool_scratch names a host-side stand-in, not device memory. The device address is looked
+// up once per device with cudaGetSymbolAddress (with that device current) and cached.
+// ---------------------------------------------------------------------------------------------------------------
+static __device__ __align__(256) float g_gpool_scratch[KC_GPOOL_NOALLOC_MAX_FLOATS];
+
+namespace {
+std::mutex g_scratch_mu;
+float* g_scratch_addr[128] = {nullptr};
+
+float* gpool_scratch_for_current_device() {
+  int dev = -1;
+  KC_CUDA(cudaGetDevice(&dev));
+  if (dev < 0 || dev >= 128) kc::fail(KC_ERR_INVALID, "CUDA backend: device index out of range");
+  std::lock_guard<std::mutex> lock(g_scratch_mu);
+  if (!g_scratch_addr[dev]) {
+    void* p = nullptr;
+    KC_CUDA(cudaGetSymbolAddress(&p, g_gpool_scratch));
+    g_scratch_addr[dev] = static_cast<float*>(p);
+  }
+  return g_scratch_addr[dev];
+}
+}  // namespace
+
+extern "C" int kc_gpool_fc_noalloc(const float* d_x, const float* d_mask, int n, int c, const float* d_w, int oc,
+                                   float* d_out, void* stream) {
+  return guard_op([&] {
+    kc::check_gpool_args(d_x, d_mask, n, c, d_w, oc, d_out);
+    if ((long long)n * 3 * c > KC_GPOOL_NOALLOC_MAX_FLOATS)
+      kc::fail(KC_ERR_INVALID, "CUDA backend: kc_gpool_fc_noalloc: n * 3 * c = " + std::to_string((long long)n * 3 * c) +
+                                   " floats exceeds its fixed scratch of " +
+                                   std::to_string(KC_GPOOL_NOALLOC_MAX_FLOATS) + " floats; use kc_gpool_fc");
+    float* scratch = gpool_scratch_for_current_device();
+    // every entry of the scratch that the matmul reads is written by the pooling kernel first: nothing to clear
+    kc::launch_gpool_fc(d_x, d_mask, n, c, d_w, oc, d_out, scratch, static_cast<cudaStream_t>(stream));
+  });
+}
 
 extern "C" int kc_gpool_fc(const float* d_x, const float* d_mask, int n, int c, const float* d_w, int oc,
                            float* d_out, void* stream) {

@@ -89,7 +89,9 @@ _SIGS = {
     "kc_handle_launch_count": ([P, I, ctypes.POINTER(I)], I),
     "kc_copy_with_symmetry": ([FP, FP, I, I, I, I, I, I], I),
     "kc_gpool_fc": ([P, P, I, I, P, I, P, P], I),
+    "kc_gpool_fc_noalloc": ([P, P, I, I, P, I, P, P], I),
 }
+GPOOL_NOALLOC_MAX_FLOATS = 262144
 
 
 def lib():
@@ -287,6 +289,11 @@ class Handle:
 def gpool_fc(d_x: int, d_mask: int, n: int, c: int, d_w: int, oc: int, d_out: int, stream: int = 0):
     """kc_gpool_fc on device pointers (masked global pooling + gpool-to-bias matmul)."""
     _check(lib().kc_gpool_fc(d_x, d_mask, n, c, d_w, oc, d_out, stream or None))
+
+
+def gpool_fc_noalloc(d_x: int, d_mask: int, n: int, c: int, d_w: int, oc: int, d_out: int, stream: int = 0):
+    """kc_gpool_fc_noalloc: the same operator with its scratch in a fixed device array (no allocation)."""
+    _check(lib().kc_gpool_fc_noalloc(d_x, d_mask, n, c, d_w, oc, d_out, stream or None))
 
 
 def copy_with_symmetry(src: np.ndarray, n: int, h: int, w: int, c: int, symmetry: int, reverse: bool) -> np.ndarray:
