@@ -20,6 +20,7 @@
 
 #include "common.h"
 #include "attention.cuh"
+#include "gemm_pair.cuh"
 #include "kernels.cuh"
 
 namespace kc {
@@ -56,6 +57,24 @@ CUtensorMap make_map(const void* base, bool bf16, int cols, int rows, int box_ro
   CUresult r = encode_fn()(&map, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2,
                            const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
                            CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                           CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) fail(KC_ERR_CUDA, "CUDA backend: cuTensorMapEncodeTiled failed (" + std::to_string((int)r) + ")");
+  return map;
+}
+
+// A 32-row x 32-column box map with the 64-byte swizzle: the epilogue boxes (outputs and residuals) of the
+// CTA-pair GEMM.
+CUtensorMap make_box_map(const void* base, bool bf16, int cols, int rows) {
+  CUtensorMap map;
+  cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)cols * 2};
+  cuuint32_t box[2] = {32, 32};
+  cuuint32_t estr[2] = {1, 1};
+  if ((reinterpret_cast<uintptr_t>(base) & 15) != 0 || cols % 32 != 0)
+    fail(KC_ERR_INVALID, "CUDA backend: epilogue box operand not aligned");
+  CUresult r = encode_fn()(&map, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2,
+                           const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                           CU_TENSOR_MAP_SWIZZLE_64B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) fail(KC_ERR_CUDA, "CUDA backend: cuTensorMapEncodeTiled failed (" + std::to_string((int)r) + ")");
   return map;
@@ -118,6 +137,50 @@ void launch_tc(bool prepare, bool rf32, bool win, int bn, int grid, cudaStream_t
   }
   if (win) launch_tc_rf<T, false, true>(prepare, bn, grid, s, a, b, p);
   else launch_tc_rf<T, false, false>(prepare, bn, grid, s, a, b, p);
+}
+
+// The CTA-pair GEMM, launched as clusters of two CTAs. `prepare` (plan-build time) opts the instance into its
+// shared memory and returns how many pairs fit on the device at once; otherwise launches `pairs` pairs.
+struct PairMaps {
+  CUtensorMap a, b, res, raw, act;
+};
+
+template <typename T, int BN>
+int launch_pair_bn(bool prepare, int pairs, cudaStream_t s, const PairMaps& m, const GemmParams& p) {
+  using C = PairCfg<BN>;
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeClusterDimension;
+  at[0].val.clusterDim.x = 2;
+  at[0].val.clusterDim.y = 1;
+  at[0].val.clusterDim.z = 1;
+  cfg.blockDim = dim3(C::THREADS);
+  cfg.dynamicSmemBytes = C::SMEM;
+  cfg.stream = s;
+  cfg.attrs = at;
+  cfg.numAttrs = 1;
+  if (prepare) {
+    allow_smem(gemm_pair_kernel<T, BN>, C::SMEM);
+    cfg.gridDim = dim3(2);
+    int clusters = 0;
+    KC_CUDA(cudaOccupancyMaxActiveClusters(&clusters, gemm_pair_kernel<T, BN>, &cfg));
+    if (clusters <= 0) fail(KC_ERR_CUDA, "CUDA backend: no CTA pair of the trunk GEMM fits on this device");
+    return clusters;
+  }
+  cfg.gridDim = dim3(2 * pairs);
+  KC_CUDA(cudaLaunchKernelEx(&cfg, gemm_pair_kernel<T, BN>, m.a, m.b, m.res, m.raw, m.act, p));
+  return pairs;
+}
+
+template <typename T>
+int launch_pair(bool prepare, int bn, int pairs, cudaStream_t s, const PairMaps& m, const GemmParams& p) {
+  switch (bn) {
+    case 128: return launch_pair_bn<T, 128>(prepare, pairs, s, m, p);
+    case 192: return launch_pair_bn<T, 192>(prepare, pairs, s, m, p);
+    case 256: return launch_pair_bn<T, 256>(prepare, pairs, s, m, p);
+    default: fail(KC_ERR_INVALID, "CUDA backend: unsupported pair tile width " + std::to_string(bn));
+  }
+  return 0;
 }
 
 // How a windowed A start that is not a multiple of 8 rows is described to tcgen05. Measured on B200: the 128 B
@@ -355,6 +418,25 @@ struct Builder {
     int rope_table_stride = 0, rope_q_cols = 0, rope_rot_cols = 0, head_dim = 0, rope_group = 1;
   };
 
+  // Tile width of the CTA-pair kernel for this GEMM, or 0 when the one-CTA kernel must run it: one segment of
+  // 2-byte raw / batch-norm-activation outputs (with or without a 2-byte residual) on 32-column-aligned operands.
+  // KATAGO_CUDA_PAIR=0 sends every GEMM to the one-CTA kernel.
+  int pair_tile(const Spec& s, const GemmParams& p) const {
+    const char* e = std::getenv("KATAGO_CUDA_PAIR");
+    if (e && e[0] == '0') return 0;
+    if (s.stem || s.mode != MODE_SEGMENTS || p.nseg != 1) return 0;
+    const int f = p.seg[0].flags;
+    if ((f & ~(EPI_RAW | EPI_ACT | EPI_RESIDUAL)) || !(f & (EPI_RAW | EPI_ACT))) return 0;
+    const Seg& g = s.segs[0];
+    for (const Tensor* t : {&g.res, &g.raw, &g.actout})
+      if (t->p && (t->f32 || t->ld % 32 != 0)) return 0;
+    if (g.res_c0 % 32 || g.raw_c0 % 32 || g.act_c0 % 32) return 0;
+    if ((f & EPI_ACT) && s.N > PairCfg<256>::PARAM_COLS) return 0;
+    for (int bn : {256, 192, 128})
+      if (s.N % bn == 0) return bn;
+    return 0;
+  }
+
   static int pick_bn(int N, int mult) {
     const int cands[] = {256, 192, 128, 96, 64, 48, 32, 16};
     for (int c : cands)
@@ -452,6 +534,28 @@ struct Builder {
         p.win_rows = round_up(128 + 2 * halo, 8);
         p.win_base_mode = win_base_mode();
         if (p.win_rows > TcCfg<256, true>::WIN_MAX_ROWS) win = false;
+      }
+      if (s.cin % 64 != 0) fail(KC_ERR_INVALID, "CUDA backend: GEMM input channels not padded");
+      if (const int pbn = win ? 0 : pair_tile(s, p)) {
+        // the trunk's one-segment GEMMs: CTA-pair kernel with TMA-staged epilogue boxes
+        const Seg& g = s.segs[0];
+        const Tensor& out0 = g.raw.p ? g.raw : g.actout;
+        auto box = [&](const Tensor& t) { return make_box_map(t.p ? t.p : out0.p, bf16, t.p ? t.ld : out0.ld,
+                                                              rows_for(t.p ? t : out0)); };
+        PairMaps pm;
+        pm.a = make_map(s.A.p, bf16, s.A.ld, a_rows, 128);
+        pm.b = make_map(dW, bf16, K, s.N, pbn / 2);
+        pm.res = box(g.res);
+        pm.raw = box(g.raw);
+        pm.act = box(g.actout);
+        const int max_pairs = launch_pair<T>(true, pbn, 0, 0, pm, p);
+        add(s.cls, [=](cudaStream_t st, int n) {
+          GemmParams q = p;
+          q.g.rows = n * brows;
+          const int tiles = ((q.g.rows + 255) / 256) * (q.n_total / pbn);
+          launch_pair<T>(false, pbn, std::min(tiles, max_pairs), st, pm, q);
+        });
+        return;
       }
       CUtensorMap ta = make_map(s.A.p, bf16, s.A.ld, a_rows, win ? p.win_rows : 128);
       CUtensorMap tb = make_map(dW, bf16, K, s.N, bn);

@@ -689,22 +689,39 @@ __global__ void __launch_bounds__(TcCfg<BN, WIN>::THREADS, 1)
             }
           }
         } else {
-          for (int kb = 0; kb < KB; kb++) {
-            if (!mbar_wait(&full[stage], phase, p.err, DEV_TIMEOUT_MMA) || *abort_flag) {
-              ok = false;
-              break;
+          // Two K-blocks (8 MMAs) per barrier wait and commit: tcgen05.mma issue blocks once a few MMAs are
+          // queued, so the wait / commit latency between groups would otherwise idle the tensor pipe; with 4 MMAs
+          // per group it cost a third of the throughput, with 8 under 2%.
+          for (int kb = 0; kb < KB && ok; kb += 2) {
+            const int nk = KB - kb >= 2 ? 2 : 1;
+            int st[2];
+            uint32_t ph[2];
+            for (int j = 0; j < nk; j++) {
+              st[j] = stage;
+              ph[j] = phase;
+              if (++stage == C::STAGES) {
+                stage = 0;
+                phase ^= 1;
+              }
             }
+            for (int j = 0; j < nk; j++) {
+              if (!mbar_try_wait(&full[st[j]], ph[j]) &&
+                  (*abort_flag || !mbar_wait(&full[st[j]], ph[j], p.err, DEV_TIMEOUT_MMA))) {
+                ok = false;
+                break;
+              }
+            }
+            if (!ok) break;
             tc_fence_after();
-            const uint32_t sa = smem_u32(stages + stage * C::STAGE_BYTES);
-            const uint32_t sb = sa + C::A_BYTES;
+            for (int j = 0; j < nk; j++) {
+              const uint32_t sa = smem_u32(stages + st[j] * C::STAGE_BYTES);
+              const uint32_t sb = sa + C::A_BYTES;
 #pragma unroll
-            for (int k = 0; k < 4; k++)
-              umma_f16(d_tmem, make_sw128_desc(sa + k * 32), make_sw128_desc(sb + k * 32), IDESC, (kb | k) != 0);
-            umma_commit(&empty[stage]);
-            if (++stage == C::STAGES) {
-              stage = 0;
-              phase ^= 1;
+              for (int k = 0; k < 4; k++)
+                umma_f16(d_tmem, make_sw128_desc(sa + k * 32), make_sw128_desc(sb + k * 32), IDESC,
+                         (kb | j | k) != 0);
             }
+            for (int j = 0; j < nk; j++) umma_commit(&empty[st[j]]);
           }
         }
         if (!ok) break;
@@ -724,12 +741,15 @@ __global__ void __launch_bounds__(TcCfg<BN, WIN>::THREADS, 1)
     const int row_in_tile = q * 32 + lane;
     const GemmParams& sp = *s_params;
     int local = 0;
+    RowInfo ri_next = row_info(sp.g, (blockIdx.x / n_tiles) * 128 + row_in_tile);
     for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, local++) {
       const int acc = local & 1;
       const uint32_t acc_phase = (local >> 1) & 1;
-      const int m0 = (tile / n_tiles) * 128;
       const int n0 = (tile % n_tiles) * BN;
-      const RowInfo ri = row_info(sp.g, m0 + row_in_tile);  // its mask load overlaps the wait
+      const RowInfo ri = ri_next;
+      // the next tile's row (and its mask load) is fetched now, so the load overlaps this tile's epilogue
+      const int tnext = tile + gridDim.x;
+      if (tnext < num_tiles) ri_next = row_info(sp.g, (tnext / n_tiles) * 128 + row_in_tile);
       if (!mbar_wait(&tfull[acc], acc_phase, p.err, DEV_TIMEOUT_EPILOGUE) || *abort_flag) {
         *abort_flag = 1;
         break;

@@ -1,0 +1,398 @@
+// The trunk's convolution / linear GEMM on a CTA pair: tcgen05 MMAs of M = 256 rows (cta_group::2, 128 rows per
+// CTA), operand tiles by TMA in 128-channel pipeline stages, accumulators in TMEM, and an epilogue that stages each
+// 32 x 32 output box in shared memory and writes it with a TMA store (residuals arrive the same way, by TMA loads).
+//
+// It computes what gemm_tc_kernel computes for one-segment GEMMs with 2-byte outputs and residuals
+// (the raw / residual / batch-norm-activation epilogue of bin2onnx.py residual_block :1243-1248 and
+// nested_bottleneck_block :1263-1269): y = A * W^T (+ residual); raw = y * mask; act = act(y * scale + bias) * mask.
+//
+// Why the layout is what it is (measured on B200):
+//  * tcgen05.mma issue blocks the issuing thread once about four MMAs are queued, and each barrier wait + commit
+//    costs it a few hundred cycles, so a stage carries two 64-channel K-blocks (8 MMAs per wait / commit);
+//  * M = 256 over a CTA pair halves the B (weight) bytes each SM loads and stages, which leaves the shared memory
+//    for two such stages plus the epilogue's staging boxes;
+//  * row-per-thread global stores cost one memory transaction per 16 bytes; a TMA store writes a whole box.
+#pragma once
+
+#include "gemm.cuh"
+
+namespace kc {
+
+template <int BN>
+struct PairCfg {
+  static_assert(BN % 64 == 0 && BN >= 64 && BN <= 256, "pair tile width");
+  static constexpr int BH = BN / 2;               // B rows (output columns) staged by each CTA of the pair
+  static constexpr int A_BYTES = 128 * 64 * 2;    // one 64-channel K-block of this CTA's 128 rows
+  static constexpr int B_BYTES = BH * 64 * 2;     // one K-block of this CTA's half of the weights
+  static constexpr int KB_BYTES = A_BYTES + B_BYTES;
+  static constexpr int KBS = 2;                   // K-blocks per pipeline stage
+  static constexpr int STAGE_BYTES = KBS * KB_BYTES;
+  static constexpr int EPI_WARPS = 8;             // two per TMEM lane quarter, splitting the tile's columns
+  static constexpr int WARP_COLS = BN / 2;
+  static constexpr int CHUNKS = WARP_COLS / 32;   // 32-column boxes per warp and tile
+  static constexpr int BOX_BYTES = 32 * 32 * 2;   // 32 rows x 32 columns of a 2-byte type (64-byte swizzle)
+  static constexpr int EPI_WARP_BYTES = 4 * BOX_BYTES;  // raw box, act box, two residual boxes
+  static constexpr int EPI_BYTES = EPI_WARPS * EPI_WARP_BYTES;
+  static constexpr int PARAM_COLS = 768;          // per-column BN scale / bias in shared memory
+  static constexpr int PARAM_BYTES = 2 * PARAM_COLS * 4;
+  static constexpr int PCOPY_BYTES = 1024;
+  static constexpr int BAR_BYTES = 512;
+  static constexpr int SMEM_LIMIT = 227 * 1024;
+  static constexpr int FIXED = 1024 /*align slack*/ + EPI_BYTES + PARAM_BYTES + PCOPY_BYTES + BAR_BYTES;
+  static constexpr int FIT = (SMEM_LIMIT - FIXED) / STAGE_BYTES;
+  static constexpr int STAGES = FIT > 4 ? 4 : FIT;
+  static_assert(STAGES >= 2, "pair pipeline depth");
+  static constexpr int SMEM = FIXED + STAGES * STAGE_BYTES;
+  static constexpr uint32_t ACC_COLS = BN <= 64 ? 64 : BN <= 128 ? 128 : 256;
+  static constexpr uint32_t TMEM_COLS = 2 * ACC_COLS;
+  static constexpr int THREADS = 64 + 32 * EPI_WARPS;
+};
+
+// The 16-byte chunk `j` (0..3) of row `r` of a 32 x 64-byte box written by TMA with CU_TENSOR_MAP_SWIZZLE_64B:
+// the chunk index is XORed with address bits 7-8, i.e. with (r / 2) % 4 for 64-byte rows. Thread r of a warp
+// touching chunk j of its own row hits 8 distinct 16-byte bank groups per 8 threads: no conflicts.
+__device__ __forceinline__ uint32_t sw64_off(int r, int j) { return (uint32_t)(r * 64 + ((j ^ ((r >> 1) & 3)) << 4)); }
+
+template <typename T>
+__device__ __forceinline__ uint32_t pack2(float a, float b);
+template <>
+__device__ __forceinline__ uint32_t pack2<__half>(float a, float b) {
+  __half2 h = __floats2half2_rn(a, b);
+  return *reinterpret_cast<uint32_t*>(&h);
+}
+template <>
+__device__ __forceinline__ uint32_t pack2<__nv_bfloat16>(float a, float b) {
+  __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+  return *reinterpret_cast<uint32_t*>(&h);
+}
+
+// Write 32 floats of this thread's row into a 64-byte-swizzled staging box as T.
+template <typename T>
+__device__ __forceinline__ void stage_row(uint8_t* box, int r, const float (&o)[32]) {
+#pragma unroll
+  for (int j = 0; j < 4; j++) {
+    uint4 u;
+    u.x = pack2<T>(o[8 * j + 0], o[8 * j + 1]);
+    u.y = pack2<T>(o[8 * j + 2], o[8 * j + 3]);
+    u.z = pack2<T>(o[8 * j + 4], o[8 * j + 5]);
+    u.w = pack2<T>(o[8 * j + 6], o[8 * j + 7]);
+    *reinterpret_cast<uint4*>(box + sw64_off(r, j)) = u;
+  }
+}
+
+// act(v * scale + bias) * mask over 32 columns, scale / bias from shared memory (broadcast reads).
+template <int ACT>
+__device__ __forceinline__ void pair_act(const float (&v)[32], const float* sc, const float* bi, float m,
+                                         float (&o)[32]) {
+#pragma unroll
+  for (int j = 0; j < 32; j += 16) {
+    float s[16], b[16];
+    lds16(sc + j, s);
+    lds16(bi + j, b);
+#pragma unroll
+    for (int i = 0; i < 16; i++) {
+      float t = v[j + i] * s[i];
+      t = t + b[i];
+      o[j + i] = act_fn<ACT>(t) * m;
+    }
+  }
+}
+
+template <typename T, int BN>
+__global__ void __launch_bounds__(PairCfg<BN>::THREADS, 1)
+    gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                     const __grid_constant__ CUtensorMap tmRes, const __grid_constant__ CUtensorMap tmRaw,
+                     const __grid_constant__ CUtensorMap tmAct, const __grid_constant__ GemmParams p) {
+  using C = PairCfg<BN>;
+  constexpr int fmt = std::is_same<T, __nv_bfloat16>::value ? 1 : 0;
+  constexpr uint32_t IDESC = make_idesc_f16(fmt, 256, BN);
+
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* stages = smem;
+  uint8_t* epi = stages + C::STAGES * C::STAGE_BYTES;
+  float* s_scale = reinterpret_cast<float*>(epi + C::EPI_BYTES);
+  float* s_bias = s_scale + C::PARAM_COLS;
+  GemmParams* s_params = reinterpret_cast<GemmParams*>(s_bias + C::PARAM_COLS);
+  uint64_t* full = reinterpret_cast<uint64_t*>(reinterpret_cast<uint8_t*>(s_params) + C::PCOPY_BYTES);
+  uint64_t* empty = full + C::STAGES;
+  uint64_t* tfull = empty + C::STAGES;
+  uint64_t* tempty = tfull + 2;
+  uint64_t* drain = tempty + 2;
+  uint64_t* rbar = drain + 1;  // [EPI_WARPS][2]: the residual boxes of each epilogue warp
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(rbar + 2 * C::EPI_WARPS);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  static_assert(sizeof(GemmParams) <= C::PCOPY_BYTES && sizeof(GemmParams) % 16 == 0, "parameter copy");
+  static_assert((2 * C::STAGES + 5 + 2 * C::EPI_WARPS) * 8 + 8 <= C::BAR_BYTES, "barrier area");
+  for (int i = threadIdx.x; i < (int)(sizeof(GemmParams) / 16); i += blockDim.x)
+    reinterpret_cast<uint4*>(s_params)[i] = reinterpret_cast<const uint4*>(&p)[i];
+  const int flags = p.seg[0].flags;
+  if ((flags & EPI_ACT) && p.n_total <= C::PARAM_COLS) {
+    for (int col = threadIdx.x; col < p.n_total; col += blockDim.x) {
+      s_scale[col] = p.seg[0].scale[col];
+      s_bias[col] = p.seg[0].bias[col];
+    }
+  }
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_ctarank();
+  const bool leader = rank == 0;
+  const int pair = blockIdx.x >> 1, npairs = gridDim.x >> 1;
+  const int n_tiles = p.n_total / BN;
+  const int num_tiles = ((p.g.rows + 255) / 256) * n_tiles;
+  const int kb_per_tap = p.cin / 64;
+  const int KB = p.taps * kb_per_tap;
+  const int NST = (KB + C::KBS - 1) / C::KBS;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < C::STAGES; s++) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int a = 0; a < 2; a++) {
+      mbar_init(&tfull[a], 1);
+      mbar_init(&tempty[a], 2 * C::EPI_WARPS);  // one arrival per epilogue warp of both CTAs
+    }
+    mbar_init(drain, 1);
+    for (int i = 0; i < 2 * C::EPI_WARPS; i++) mbar_init(&rbar[i], 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+    prefetch_tensormap(&tmA);
+    prefetch_tensormap(&tmB);
+  }
+  if (warp == 0) {
+    tmem_alloc_pair(tmem_slot, C::TMEM_COLS);
+    tmem_relinquish_pair();
+  }
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync();  // both CTAs' barriers exist before any cross-CTA arrive or transaction
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ---- TMA producer (both CTAs): this CTA's A rows and half of B; the bytes count on the leader's barrier
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      for (int tile = pair; tile < num_tiles && ok; tile += npairs) {
+        const int m0 = (tile / n_tiles) * 256 + (int)rank * 128;
+        const int nb = (tile % n_tiles) * BN + (int)rank * C::BH;
+        for (int st = 0; st < NST; st++) {
+          if (!mbar_try_wait(&empty[stage], phase ^ 1) &&
+              (*abort_flag || !mbar_wait(&empty[stage], phase ^ 1, p.err, DEV_TIMEOUT_PRODUCER))) {
+            ok = false;
+            *abort_flag = 1;
+            break;
+          }
+          const int kb0 = st * C::KBS;
+          const int nk = KB - kb0 < C::KBS ? KB - kb0 : C::KBS;
+          if (leader) mbar_expect_tx(&full[stage], 2u * (uint32_t)nk * C::KB_BYTES);
+          const uint32_t fb = mapa_shared(smem_u32(&full[stage]), 0);
+          uint8_t* sbase = stages + stage * C::STAGE_BYTES;
+          for (int j = 0; j < nk; j++) {
+            const int kb = kb0 + j;
+            const int tap = kb / kb_per_tap;
+            const int c0 = (kb - tap * kb_per_tap) * 64;
+            tma_load_2d_pair(sbase + j * C::KB_BYTES, &tmA, fb, c0, m0 + s_params->tap_off[tap]);
+            tma_load_2d_pair(sbase + j * C::KB_BYTES + C::A_BYTES, &tmB, fb, kb * 64, nb);
+          }
+          if (++stage == C::STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+      }
+      if (!ok) {
+        // let copies already issued land before the CTA exits (bounded)
+        unsigned long long t0 = globaltimer();
+        while (globaltimer() - t0 < 2000000ull) {
+        }
+      }
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    if (lane == 0 && leader) {
+      // ---- MMA issuer (leader CTA only): one M = 256 MMA covers both CTAs' rows
+      const uint32_t peer = 1;
+      int stage = 0;
+      uint32_t phase = 0;
+      int local = 0;
+      bool ok = true;
+      for (int tile = pair; tile < num_tiles && ok; tile += npairs, local++) {
+        const int acc = local & 1;
+        const uint32_t acc_phase = (local >> 1) & 1;
+        if (!mbar_wait(&tempty[acc], acc_phase ^ 1, p.err, DEV_TIMEOUT_MMA) || *abort_flag) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + acc * C::ACC_COLS;
+        for (int st = 0; st < NST; st++) {
+          if (!mbar_try_wait(&full[stage], phase) &&
+              (*abort_flag || !mbar_wait(&full[stage], phase, p.err, DEV_TIMEOUT_MMA))) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const int nk = KB - st * C::KBS < C::KBS ? KB - st * C::KBS : C::KBS;
+          const uint32_t sbase = smem_u32(stages + stage * C::STAGE_BYTES);
+          for (int j = 0; j < nk; j++) {
+            const uint32_t sa = sbase + j * C::KB_BYTES, sb = sa + C::A_BYTES;
+#pragma unroll
+            for (int k = 0; k < 4; k++)
+              umma_f16_pair(d_tmem, make_sw128_desc(sa + k * 32), make_sw128_desc(sb + k * 32), IDESC,
+                            (st | j | k) != 0);
+          }
+          const uint32_t eb = smem_u32(&empty[stage]);
+          umma_commit_pair(eb);
+          umma_commit_pair(mapa_shared(eb, peer));
+          if (++stage == C::STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+        if (!ok) break;
+        const uint32_t tb = smem_u32(&tfull[acc]);
+        umma_commit_pair(tb);
+        umma_commit_pair(mapa_shared(tb, peer));
+      }
+      if (!ok) {
+        *abort_flag = 1;
+        umma_commit_pair(smem_u32(drain));  // wait for MMAs in flight before TMEM is released
+        mbar_wait(drain, 0, p.err, DEV_TIMEOUT_DRAIN);
+      }
+    }
+    __syncwarp();
+  } else {
+    // ---- epilogue warps 2..9 (both CTAs): TMEM lane quarter warp % 4, column half (warp - 2) / 4
+    const int ew = warp - 2;
+    const int q = warp & 3;
+    const int h = ew >> 2;
+    uint8_t* wbuf = epi + ew * C::EPI_WARP_BYTES;
+    uint8_t* st_raw = wbuf;
+    uint8_t* st_act = wbuf + C::BOX_BYTES;
+    uint64_t* rb = rbar + 2 * ew;
+    const bool has_res = (flags & EPI_RESIDUAL) != 0;
+    const int act = p.seg[0].act;
+    const int res_c0 = p.seg[0].res_c0, raw_c0 = p.seg[0].raw_c0, act_c0 = p.seg[0].act_c0;
+    const uint32_t tempty_leader0 = mapa_shared(smem_u32(&tempty[0]), 0);
+
+    // residual boxes run one box ahead per buffer: box u (this warp's u-th 32-column chunk over its tiles) goes
+    // to buffer u % 2
+    auto res_issue = [&](int u) {
+      const int i = u / C::CHUNKS, c = u - i * C::CHUNKS;
+      const int tile = pair + i * npairs;
+      if (tile >= num_tiles) return;
+      const int mrow = (tile / n_tiles) * 256 + (int)rank * 128 + q * 32;
+      const int col = (tile % n_tiles) * BN + h * C::WARP_COLS + c * 32;
+      mbar_expect_tx(&rb[u & 1], C::BOX_BYTES);
+      tma_load_2d(wbuf + (2 + (u & 1)) * C::BOX_BYTES, &tmRes, &rb[u & 1], res_c0 + col, mrow);
+    };
+    if (has_res && lane == 0) {
+      res_issue(0);
+      res_issue(1);
+    }
+
+    int local = 0, u = 0;
+    bool ok = true;
+    for (int tile = pair; tile < num_tiles && ok; tile += npairs, local++) {
+      const int acc = local & 1;
+      const uint32_t acc_phase = (local >> 1) & 1;
+      const int mrow = (tile / n_tiles) * 256 + (int)rank * 128 + q * 32;
+      const int r = mrow + lane;
+      const float m = r < p.g.rows ? __ldg(p.g.rowmask + r) : 0.0f;
+      const int ncol0 = (tile % n_tiles) * BN + h * C::WARP_COLS;
+      if (!mbar_wait(&tfull[acc], acc_phase, p.err, DEV_TIMEOUT_EPILOGUE) || *abort_flag) {
+        *abort_flag = 1;
+        ok = false;
+        break;
+      }
+      __syncwarp();
+      tc_fence_after();
+      const uint32_t tacc = tmem_base + acc * C::ACC_COLS + ((uint32_t)(q * 32) << 16) + h * C::WARP_COLS;
+#pragma unroll 1
+      for (int c = 0; c < C::CHUNKS; c++, u++) {
+        uint32_t x[32];
+        tmem_ld32(tacc + c * 32, x);
+        tmem_wait_ld();
+        if (c == C::CHUNKS - 1) {
+          // the accumulator is in registers: hand it back to the MMA issuer before the math
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive_cluster(tempty_leader0 + acc * 8);
+        }
+        float v[32];
+#pragma unroll
+        for (int i = 0; i < 32; i++) v[i] = __uint_as_float(x[i]);
+        if (has_res) {
+          if (!mbar_wait(&rb[u & 1], (u >> 1) & 1, p.err, DEV_TIMEOUT_EPILOGUE)) {
+            *abort_flag = 1;
+            ok = false;
+            break;
+          }
+          const uint8_t* rbox = wbuf + (2 + (u & 1)) * C::BOX_BYTES;
+#pragma unroll
+          for (int j = 0; j < 4; j++) {
+            uint4 w = *reinterpret_cast<const uint4*>(rbox + sw64_off(lane, j));
+            const T* e = reinterpret_cast<const T*>(&w);
+#pragma unroll
+            for (int k = 0; k < 8; k++) v[8 * j + k] += to_f<T>(e[k]);
+          }
+          __syncwarp();
+          if (lane == 0) {
+            fence_proxy_async_smem();
+            res_issue(u + 2);
+          }
+        }
+        // the previous box's stores must have read the staging boxes before they are overwritten
+        if (lane == 0) bulk_wait_read0();
+        __syncwarp();
+        if (flags & EPI_RAW) {
+          float o[32];
+#pragma unroll
+          for (int i = 0; i < 32; i++) o[i] = v[i] * m;
+          stage_row<T>(st_raw, lane, o);
+        }
+        if (flags & EPI_ACT) {
+          float o[32];
+          const int col = ncol0 + c * 32;
+          switch (act) {
+            case 1: pair_act<1>(v, s_scale + col, s_bias + col, m, o); break;
+            case 2: pair_act<2>(v, s_scale + col, s_bias + col, m, o); break;
+            case 3: pair_act<3>(v, s_scale + col, s_bias + col, m, o); break;
+            default: pair_act<0>(v, s_scale + col, s_bias + col, m, o); break;
+          }
+          stage_row<T>(st_act, lane, o);
+        }
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+          const int col = ncol0 + c * 32;
+          if (flags & EPI_RAW) tma_store_2d(&tmRaw, st_raw, raw_c0 + col, mrow);
+          if (flags & EPI_ACT) tma_store_2d(&tmAct, st_act, act_c0 + col, mrow);
+          bulk_commit_group();
+        }
+      }
+    }
+    if (lane == 0) bulk_wait0();
+    if (!ok && has_res) {
+      // residual boxes may still be in flight towards this warp's buffers: let them land (bounded)
+      unsigned long long t0 = globaltimer();
+      while (globaltimer() - t0 < 2000000ull) {
+      }
+    }
+    __syncwarp();
+  }
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync();  // no CTA leaves while its peer may still signal its barriers
+  if (warp == 0) {
+    tc_fence_after();
+    tmem_dealloc_pair(tmem_base, C::TMEM_COLS);
+  }
+}
+
+}  // namespace kc
