@@ -145,9 +145,9 @@ struct PairMaps {
   CUtensorMap a, b, res, raw, act;
 };
 
-template <typename T, int BN>
+template <typename T, int BN, bool WIN>
 int launch_pair_bn(bool prepare, int pairs, cudaStream_t s, const PairMaps& m, const GemmParams& p) {
-  using C = PairCfg<BN>;
+  using C = PairCfg<BN, WIN>;
   cudaLaunchConfig_t cfg = {};
   cudaLaunchAttribute at[1];
   at[0].id = cudaLaunchAttributeClusterDimension;
@@ -160,27 +160,33 @@ int launch_pair_bn(bool prepare, int pairs, cudaStream_t s, const PairMaps& m, c
   cfg.attrs = at;
   cfg.numAttrs = 1;
   if (prepare) {
-    allow_smem(gemm_pair_kernel<T, BN>, C::SMEM);
+    allow_smem(gemm_pair_kernel<T, BN, WIN>, C::SMEM);
     cfg.gridDim = dim3(2);
     int clusters = 0;
-    KC_CUDA(cudaOccupancyMaxActiveClusters(&clusters, gemm_pair_kernel<T, BN>, &cfg));
+    KC_CUDA(cudaOccupancyMaxActiveClusters(&clusters, gemm_pair_kernel<T, BN, WIN>, &cfg));
     if (clusters <= 0) fail(KC_ERR_CUDA, "CUDA backend: no CTA pair of the trunk GEMM fits on this device");
     return clusters;
   }
   cfg.gridDim = dim3(2 * pairs);
-  KC_CUDA(cudaLaunchKernelEx(&cfg, gemm_pair_kernel<T, BN>, m.a, m.b, m.res, m.raw, m.act, p));
+  KC_CUDA(cudaLaunchKernelEx(&cfg, gemm_pair_kernel<T, BN, WIN>, m.a, m.b, m.res, m.raw, m.act, p));
   return pairs;
 }
 
-template <typename T>
-int launch_pair(bool prepare, int bn, int pairs, cudaStream_t s, const PairMaps& m, const GemmParams& p) {
+template <typename T, bool WIN>
+int launch_pair_w(bool prepare, int bn, int pairs, cudaStream_t s, const PairMaps& m, const GemmParams& p) {
   switch (bn) {
-    case 128: return launch_pair_bn<T, 128>(prepare, pairs, s, m, p);
-    case 192: return launch_pair_bn<T, 192>(prepare, pairs, s, m, p);
-    case 256: return launch_pair_bn<T, 256>(prepare, pairs, s, m, p);
+    case 128: return launch_pair_bn<T, 128, WIN>(prepare, pairs, s, m, p);
+    case 192: return launch_pair_bn<T, 192, WIN>(prepare, pairs, s, m, p);
+    case 256: return launch_pair_bn<T, 256, WIN>(prepare, pairs, s, m, p);
     default: fail(KC_ERR_INVALID, "CUDA backend: unsupported pair tile width " + std::to_string(bn));
   }
   return 0;
+}
+
+// win: multi-tap convolution with one A window per 64-channel chunk (PairCfg)
+template <typename T>
+int launch_pair(bool prepare, int bn, bool win, int pairs, cudaStream_t s, const PairMaps& m, const GemmParams& p) {
+  return win ? launch_pair_w<T, true>(prepare, bn, pairs, s, m, p) : launch_pair_w<T, false>(prepare, bn, pairs, s, m, p);
 }
 
 // How a windowed A start that is not a multiple of 8 rows is described to tcgen05. Measured on B200: the 128 B
@@ -542,18 +548,28 @@ struct Builder {
         const Tensor& out0 = g.raw.p ? g.raw : g.actout;
         auto box = [&](const Tensor& t) { return make_box_map(t.p ? t.p : out0.p, bf16, t.p ? t.ld : out0.ld,
                                                               rows_for(t.p ? t : out0)); };
+        // 3x3 convolutions read one A window per 64-channel chunk (KATAGO_CUDA_PAIR_WIN=0: one A tile per tap)
+        const char* pw = std::getenv("KATAGO_CUDA_PAIR_WIN");
+        bool pwin = p.taps == PairCfg<256, true>::WIN_TAPS && !(pw && pw[0] == '0');
+        if (pwin) {
+          int halo = 0;
+          for (int i = 0; i < p.taps; i++) halo = std::max(halo, std::abs(p.tap_off[i]));
+          p.halo = halo;
+          p.win_rows = round_up(128 + 2 * halo, 8);
+          if (p.win_rows > PairCfg<256, true>::WIN_MAX_ROWS) pwin = false;
+        }
         PairMaps pm;
-        pm.a = make_map(s.A.p, bf16, s.A.ld, a_rows, 128);
+        pm.a = make_map(s.A.p, bf16, s.A.ld, a_rows, pwin ? p.win_rows : 128);
         pm.b = make_map(dW, bf16, K, s.N, pbn / 2);
         pm.res = box(g.res);
         pm.raw = box(g.raw);
         pm.act = box(g.actout);
-        const int max_pairs = launch_pair<T>(true, pbn, 0, 0, pm, p);
+        const int max_pairs = launch_pair<T>(true, pbn, pwin, 0, 0, pm, p);
         add(s.cls, [=](cudaStream_t st, int n) {
           GemmParams q = p;
           q.g.rows = n * brows;
           const int tiles = ((q.g.rows + 255) / 256) * (q.n_total / pbn);
-          launch_pair<T>(false, pbn, std::min(tiles, max_pairs), st, pm, q);
+          launch_pair<T>(false, pbn, pwin, std::min(tiles, max_pairs), st, pm, q);
         });
         return;
       }

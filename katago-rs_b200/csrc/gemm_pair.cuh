@@ -8,7 +8,7 @@
 //
 // Why the layout is what it is (measured on B200):
 //  * tcgen05.mma issue blocks the issuing thread once about four MMAs are queued, and each barrier wait + commit
-//    costs it a few hundred cycles, so a stage carries two 64-channel K-blocks (8 MMAs per wait / commit);
+//    costs it a few hundred cycles, so a stage carries two or three 64-channel K-blocks (8-12 MMAs per wait);
 //  * M = 256 over a CTA pair halves the B (weight) bytes each SM loads and stages, which leaves the shared memory
 //    for two such stages plus the epilogue's staging boxes;
 //  * row-per-thread global stores cost one memory transaction per 16 bytes; a TMA store writes a whole box.
@@ -18,15 +18,23 @@
 
 namespace kc {
 
-template <int BN>
+// WIN (3x3 convolutions, 9 taps): per 64-channel chunk, each CTA loads one A window (its 128 rows plus the taps'
+// halo above and below) into a ring of two, and every tap's MMA reads its 128 rows at the tap's row offset inside
+// the window; the pipeline stages then carry only weight boxes (three taps per stage: 12 MMAs per wait). This cuts the TMA bytes of a
+// 3x3 convolution's K-block from 28 KB to about 14 KB per CTA, below what TMA delivers per SM.
+template <int BN, bool WIN = false>
 struct PairCfg {
   static_assert(BN % 64 == 0 && BN >= 64 && BN <= 256, "pair tile width");
   static constexpr int BH = BN / 2;               // B rows (output columns) staged by each CTA of the pair
   static constexpr int A_BYTES = 128 * 64 * 2;    // one 64-channel K-block of this CTA's 128 rows
   static constexpr int B_BYTES = BH * 64 * 2;     // one K-block of this CTA's half of the weights
-  static constexpr int KB_BYTES = A_BYTES + B_BYTES;
-  static constexpr int KBS = 2;                   // K-blocks per pipeline stage
+  static constexpr int KB_BYTES = (WIN ? 0 : A_BYTES) + B_BYTES;  // one K-block's slot in a stage
+  static constexpr int KBS = WIN ? 3 : 2;         // K-blocks per pipeline stage (WIN: a row of three taps)
+  static constexpr int WIN_TAPS = 9;
   static constexpr int STAGE_BYTES = KBS * KB_BYTES;
+  static constexpr int WIN_MAX_ROWS = 176;        // 128 rows + a halo of up to 24 rows on each side
+  static constexpr int A_WIN_BYTES = WIN_MAX_ROWS * 128;
+  static constexpr int A_RING_BYTES = WIN ? 2 * A_WIN_BYTES : 0;
   static constexpr int EPI_WARPS = 8;             // two per TMEM lane quarter, splitting the tile's columns
   static constexpr int WARP_COLS = BN / 2;
   static constexpr int CHUNKS = WARP_COLS / 32;   // 32-column boxes per warp and tile
@@ -38,7 +46,8 @@ struct PairCfg {
   static constexpr int PCOPY_BYTES = 1024;
   static constexpr int BAR_BYTES = 512;
   static constexpr int SMEM_LIMIT = 227 * 1024;
-  static constexpr int FIXED = 1024 /*align slack*/ + EPI_BYTES + PARAM_BYTES + PCOPY_BYTES + BAR_BYTES;
+  static constexpr int FIXED =
+      1024 /*align slack*/ + A_RING_BYTES + EPI_BYTES + PARAM_BYTES + PCOPY_BYTES + BAR_BYTES;
   static constexpr int FIT = (SMEM_LIMIT - FIXED) / STAGE_BYTES;
   static constexpr int STAGES = FIT > 4 ? 4 : FIT;
   static_assert(STAGES >= 2, "pair pipeline depth");
@@ -98,18 +107,19 @@ __device__ __forceinline__ void pair_act(const float (&v)[32], const float* sc, 
   }
 }
 
-template <typename T, int BN>
-__global__ void __launch_bounds__(PairCfg<BN>::THREADS, 1)
+template <typename T, int BN, bool WIN>
+__global__ void __launch_bounds__(PairCfg<BN, WIN>::THREADS, 1)
     gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                      const __grid_constant__ CUtensorMap tmRes, const __grid_constant__ CUtensorMap tmRaw,
                      const __grid_constant__ CUtensorMap tmAct, const __grid_constant__ GemmParams p) {
-  using C = PairCfg<BN>;
+  using C = PairCfg<BN, WIN>;
   constexpr int fmt = std::is_same<T, __nv_bfloat16>::value ? 1 : 0;
   constexpr uint32_t IDESC = make_idesc_f16(fmt, 256, BN);
 
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t* stages = smem;
+  uint8_t* awin = smem;  // WIN: the two A windows
+  uint8_t* stages = smem + C::A_RING_BYTES;
   uint8_t* epi = stages + C::STAGES * C::STAGE_BYTES;
   float* s_scale = reinterpret_cast<float*>(epi + C::EPI_BYTES);
   float* s_bias = s_scale + C::PARAM_COLS;
@@ -120,11 +130,13 @@ __global__ void __launch_bounds__(PairCfg<BN>::THREADS, 1)
   uint64_t* tempty = tfull + 2;
   uint64_t* drain = tempty + 2;
   uint64_t* rbar = drain + 1;  // [EPI_WARPS][2]: the residual boxes of each epilogue warp
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(rbar + 2 * C::EPI_WARPS);
+  uint64_t* afull = rbar + 2 * C::EPI_WARPS;  // WIN: A window ring
+  uint64_t* aempty = afull + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(aempty + 2);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   static_assert(sizeof(GemmParams) <= C::PCOPY_BYTES && sizeof(GemmParams) % 16 == 0, "parameter copy");
-  static_assert((2 * C::STAGES + 5 + 2 * C::EPI_WARPS) * 8 + 8 <= C::BAR_BYTES, "barrier area");
+  static_assert((2 * C::STAGES + 9 + 2 * C::EPI_WARPS) * 8 + 8 <= C::BAR_BYTES, "barrier area");
   for (int i = threadIdx.x; i < (int)(sizeof(GemmParams) / 16); i += blockDim.x)
     reinterpret_cast<uint4*>(s_params)[i] = reinterpret_cast<const uint4*>(&p)[i];
   const int flags = p.seg[0].flags;
@@ -156,6 +168,10 @@ __global__ void __launch_bounds__(PairCfg<BN>::THREADS, 1)
     }
     mbar_init(drain, 1);
     for (int i = 0; i < 2 * C::EPI_WARPS; i++) mbar_init(&rbar[i], 1);
+    for (int a = 0; a < 2; a++) {
+      mbar_init(&afull[a], 1);
+      mbar_init(&aempty[a], 1);
+    }
     *abort_flag = 0;
     fence_mbar_init();
     prefetch_tensormap(&tmA);
@@ -177,31 +193,60 @@ __global__ void __launch_bounds__(PairCfg<BN>::THREADS, 1)
       int stage = 0;
       uint32_t phase = 0;
       bool ok = true;
+      int as = 0;
+      uint32_t aph = 0;
+      // wait for a ring slot this CTA may refill; false (and abort) on a timeout
+      auto slot_free = [&](uint64_t* bar, uint32_t parity) {
+        if (mbar_try_wait(bar, parity)) return true;
+        if (!*abort_flag && mbar_wait(bar, parity, p.err, DEV_TIMEOUT_PRODUCER)) return true;
+        *abort_flag = 1;
+        return false;
+      };
       for (int tile = pair; tile < num_tiles && ok; tile += npairs) {
         const int m0 = (tile / n_tiles) * 256 + (int)rank * 128;
         const int nb = (tile % n_tiles) * BN + (int)rank * C::BH;
-        for (int st = 0; st < NST; st++) {
-          if (!mbar_try_wait(&empty[stage], phase ^ 1) &&
-              (*abort_flag || !mbar_wait(&empty[stage], phase ^ 1, p.err, DEV_TIMEOUT_PRODUCER))) {
-            ok = false;
-            *abort_flag = 1;
-            break;
+        if constexpr (WIN) {
+          for (int ch = 0; ch < kb_per_tap && ok; ch++) {
+            if (!(ok = slot_free(&aempty[as], aph ^ 1))) break;
+            if (leader) mbar_expect_tx(&afull[as], 2u * (uint32_t)p.win_rows * 128u);
+            tma_load_2d_pair(awin + as * C::A_WIN_BYTES, &tmA, mapa_shared(smem_u32(&afull[as]), 0), ch * 64,
+                             m0 - p.halo);
+            if (++as == 2) {
+              as = 0;
+              aph ^= 1;
+            }
+            for (int t0 = 0; t0 < C::WIN_TAPS; t0 += C::KBS) {
+              if (!(ok = slot_free(&empty[stage], phase ^ 1))) break;
+              if (leader) mbar_expect_tx(&full[stage], 2u * C::KBS * C::B_BYTES);
+              const uint32_t fb = mapa_shared(smem_u32(&full[stage]), 0);
+              for (int j = 0; j < C::KBS; j++)
+                tma_load_2d_pair(stages + stage * C::STAGE_BYTES + j * C::KB_BYTES, &tmB, fb,
+                                 (t0 + j) * p.cin + ch * 64, nb);
+              if (++stage == C::STAGES) {
+                stage = 0;
+                phase ^= 1;
+              }
+            }
           }
-          const int kb0 = st * C::KBS;
-          const int nk = KB - kb0 < C::KBS ? KB - kb0 : C::KBS;
-          if (leader) mbar_expect_tx(&full[stage], 2u * (uint32_t)nk * C::KB_BYTES);
-          const uint32_t fb = mapa_shared(smem_u32(&full[stage]), 0);
-          uint8_t* sbase = stages + stage * C::STAGE_BYTES;
-          for (int j = 0; j < nk; j++) {
-            const int kb = kb0 + j;
-            const int tap = kb / kb_per_tap;
-            const int c0 = (kb - tap * kb_per_tap) * 64;
-            tma_load_2d_pair(sbase + j * C::KB_BYTES, &tmA, fb, c0, m0 + s_params->tap_off[tap]);
-            tma_load_2d_pair(sbase + j * C::KB_BYTES + C::A_BYTES, &tmB, fb, kb * 64, nb);
-          }
-          if (++stage == C::STAGES) {
-            stage = 0;
-            phase ^= 1;
+        } else {
+          for (int st = 0; st < NST; st++) {
+            if (!(ok = slot_free(&empty[stage], phase ^ 1))) break;
+            const int kb0 = st * C::KBS;
+            const int nk = KB - kb0 < C::KBS ? KB - kb0 : C::KBS;
+            if (leader) mbar_expect_tx(&full[stage], 2u * (uint32_t)nk * C::KB_BYTES);
+            const uint32_t fb = mapa_shared(smem_u32(&full[stage]), 0);
+            uint8_t* sbase = stages + stage * C::STAGE_BYTES;
+            for (int j = 0; j < nk; j++) {
+              const int kb = kb0 + j;
+              const int tap = kb / kb_per_tap;
+              const int c0 = (kb - tap * kb_per_tap) * 64;
+              tma_load_2d_pair(sbase + j * C::KB_BYTES, &tmA, fb, c0, m0 + s_params->tap_off[tap]);
+              tma_load_2d_pair(sbase + j * C::KB_BYTES + C::A_BYTES, &tmB, fb, kb * 64, nb);
+            }
+            if (++stage == C::STAGES) {
+              stage = 0;
+              phase ^= 1;
+            }
           }
         }
       }
@@ -219,8 +264,16 @@ __global__ void __launch_bounds__(PairCfg<BN>::THREADS, 1)
       const uint32_t peer = 1;
       int stage = 0;
       uint32_t phase = 0;
+      int as = 0;
+      uint32_t aph = 0;
       int local = 0;
       bool ok = true;
+      // WIN: byte offset of each tap's 128 rows inside the window (halo + tap row offset; any row works: the
+      // 128-byte swizzle follows the absolute address, so the descriptors' base offset stays 0). Held in registers:
+      // a shared-memory read between a commit and the next MMAs stalls the issuing thread.
+      uint32_t win_off[C::WIN_TAPS];
+#pragma unroll
+      for (int t = 0; t < C::WIN_TAPS; t++) win_off[t] = WIN ? (uint32_t)(p.halo + s_params->tap_off[t]) * 128u : 0u;
       for (int tile = pair; tile < num_tiles && ok; tile += npairs, local++) {
         const int acc = local & 1;
         const uint32_t acc_phase = (local >> 1) & 1;
@@ -230,28 +283,65 @@ __global__ void __launch_bounds__(PairCfg<BN>::THREADS, 1)
         }
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + acc * C::ACC_COLS;
-        for (int st = 0; st < NST; st++) {
-          if (!mbar_try_wait(&full[stage], phase) &&
-              (*abort_flag || !mbar_wait(&full[stage], phase, p.err, DEV_TIMEOUT_MMA))) {
-            ok = false;
-            break;
-          }
-          tc_fence_after();
-          const int nk = KB - st * C::KBS < C::KBS ? KB - st * C::KBS : C::KBS;
-          const uint32_t sbase = smem_u32(stages + stage * C::STAGE_BYTES);
-          for (int j = 0; j < nk; j++) {
-            const uint32_t sa = sbase + j * C::KB_BYTES, sb = sa + C::A_BYTES;
+        auto data_ready = [&](uint64_t* bar, uint32_t parity) {
+          if (mbar_try_wait(bar, parity)) return true;
+          return !*abort_flag && mbar_wait(bar, parity, p.err, DEV_TIMEOUT_MMA);
+        };
+        // the pair's MMAs have read this stage: both CTAs may refill it
+        auto release = [&](uint64_t* bar) {
+          const uint32_t b = smem_u32(bar);
+          umma_commit_pair(b);
+          umma_commit_pair(mapa_shared(b, peer));
+        };
+        if constexpr (WIN) {
+          for (int ch = 0; ch < kb_per_tap && ok; ch++) {
+            if (!(ok = data_ready(&afull[as], aph))) break;
+            const uint32_t swin = smem_u32(awin + as * C::A_WIN_BYTES);
 #pragma unroll
-            for (int k = 0; k < 4; k++)
-              umma_f16_pair(d_tmem, make_sw128_desc(sa + k * 32), make_sw128_desc(sb + k * 32), IDESC,
-                            (st | j | k) != 0);
+            for (int g = 0; g < C::WIN_TAPS / C::KBS; g++) {
+              if (!(ok = data_ready(&full[stage], phase))) break;
+              tc_fence_after();
+              const uint32_t sbase = smem_u32(stages + stage * C::STAGE_BYTES);
+#pragma unroll
+              for (int j = 0; j < C::KBS; j++) {
+                const uint32_t sa = swin + win_off[g * C::KBS + j];
+                const uint32_t sb = sbase + j * C::KB_BYTES;
+#pragma unroll
+                for (int k = 0; k < 4; k++)
+                  umma_f16_pair(d_tmem, make_sw128_desc(sa + k * 32), make_sw128_desc(sb + k * 32), IDESC,
+                                (ch | g | j | k) != 0);
+              }
+              release(&empty[stage]);
+              if (++stage == C::STAGES) {
+                stage = 0;
+                phase ^= 1;
+              }
+            }
+            if (!ok) break;
+            release(&aempty[as]);
+            if (++as == 2) {
+              as = 0;
+              aph ^= 1;
+            }
           }
-          const uint32_t eb = smem_u32(&empty[stage]);
-          umma_commit_pair(eb);
-          umma_commit_pair(mapa_shared(eb, peer));
-          if (++stage == C::STAGES) {
-            stage = 0;
-            phase ^= 1;
+        } else {
+          for (int st = 0; st < NST; st++) {
+            if (!(ok = data_ready(&full[stage], phase))) break;
+            tc_fence_after();
+            const int nk = KB - st * C::KBS < C::KBS ? KB - st * C::KBS : C::KBS;
+            const uint32_t sbase = smem_u32(stages + stage * C::STAGE_BYTES);
+            for (int j = 0; j < nk; j++) {
+              const uint32_t sa = sbase + j * C::KB_BYTES, sb = sa + C::A_BYTES;
+#pragma unroll
+              for (int k = 0; k < 4; k++)
+                umma_f16_pair(d_tmem, make_sw128_desc(sa + k * 32), make_sw128_desc(sb + k * 32), IDESC,
+                              (st | j | k) != 0);
+            }
+            release(&empty[stage]);
+            if (++stage == C::STAGES) {
+              stage = 0;
+              phase ^= 1;
+            }
           }
         }
         if (!ok) break;
