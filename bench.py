@@ -9,7 +9,7 @@ crates/katago-nn-burn/examples/bench.rs:27-32: plane 0 = mask, stones at ~30%, g
 
 Our arm prints one JSON line with `value` (device-resident inputs, CUDA events on the handle's stream, L2 flushed
 between timed steps), `e2e` (the same through the C ABI's host path kc_enqueue / kc_wait: pinned-host inputs copied
-in and output rows copied back every step), the roofline of the dominant kernel class (the 3x3-conv tcgen05 GEMM)
+in and output rows copied back every step), the roofline of the dominant kernel class (the 3x3-conv CTA-pair tcgen05 GEMM)
 and a CPU baseline (the CPU oracle, rank 0 at N = 1). Under torchrun each rank drives its own GPU with its own
 batch (weak scaling, no collective on the data path); the time is the max over ranks.
 
@@ -33,8 +33,8 @@ sys.path.insert(0, os.path.join(REPO, "katago-rs_b200", "python"))
 METRIC = "b18c384nbt evals/s at batch 256 per GPU"
 UNIT = "evals/s"
 # DRAM bytes (read + write) per 3x3-convolution GEMM launch at batch 256, from the full ncu capture summarised in
-# profiles/gemm_tc_b18c384nbt_batch256.md (mean of the two 3x3 launches captured).
-CONV3_DRAM_BYTES_PER_LAUNCH = 73.6e6
+# profiles/gemm_pair_b18c384nbt_batch256.md (mean of the two 3x3 launches captured).
+CONV3_DRAM_BYTES_PER_LAUNCH = 74.8e6
 
 
 def parse():
@@ -316,7 +316,7 @@ def run_ours(args):
             "roofline": {"bound": "tensor", "achieved": achieved, "peak": sustained, "unit": "TFLOP/s", "frac": frac,
                          "traffic": CONV3_DRAM_BYTES_PER_LAUNCH if args.net == "b18c384nbt" and args.batch == 256
                          else None,
-                         "kernel": "gemm_tc_kernel (3x3 conv implicit GEMM)",
+                         "kernel": "gemm_pair_kernel (3x3 conv: CTA-pair tcgen05 implicit GEMM, windowed A)",
                          "peak_kind": f"{src} bf16 sustained"},
             "kernels": other,
             "profiled_ms_per_step": prof_ms / args.steps,
