@@ -424,20 +424,29 @@ struct Builder {
     int rope_table_stride = 0, rope_q_cols = 0, rope_rot_cols = 0, head_dim = 0, rope_group = 1;
   };
 
-  // Tile width of the CTA-pair kernel for this GEMM, or 0 when the one-CTA kernel must run it: one segment of
-  // 2-byte raw / batch-norm-activation outputs (with or without a 2-byte residual) on 32-column-aligned operands.
-  // KATAGO_CUDA_PAIR=0 sends every GEMM to the one-CTA kernel.
+  // Tile width of the CTA-pair kernel for this GEMM, or 0 when the one-CTA kernel must run it: one or two column
+  // segments of 2-byte raw / batch-norm-activation outputs (a 2-byte residual only with one segment), each kind of
+  // output in at most one segment, on 32-column-aligned operands. KATAGO_CUDA_PAIR=0 sends every GEMM to the
+  // one-CTA kernel.
   int pair_tile(const Spec& s, const GemmParams& p) const {
     const char* e = std::getenv("KATAGO_CUDA_PAIR");
     if (e && e[0] == '0') return 0;
-    if (s.stem || s.mode != MODE_SEGMENTS || p.nseg != 1) return 0;
-    const int f = p.seg[0].flags;
-    if ((f & ~(EPI_RAW | EPI_ACT | EPI_RESIDUAL)) || !(f & (EPI_RAW | EPI_ACT))) return 0;
-    const Seg& g = s.segs[0];
-    for (const Tensor* t : {&g.res, &g.raw, &g.actout})
-      if (t->p && (t->f32 || t->ld % 32 != 0)) return 0;
-    if (g.res_c0 % 32 || g.raw_c0 % 32 || g.act_c0 % 32) return 0;
-    if ((f & EPI_ACT) && s.N > PairCfg<256>::PARAM_COLS) return 0;
+    if (s.stem || s.mode != MODE_SEGMENTS || p.nseg < 1 || p.nseg > 2) return 0;
+    int n_raw = 0, n_act = 0, n_res = 0;
+    for (int i = 0; i < p.nseg; i++) {
+      const int f = p.seg[i].flags;
+      if ((f & ~(EPI_RAW | EPI_ACT | EPI_RESIDUAL)) || !(f & (EPI_RAW | EPI_ACT))) return 0;
+      n_raw += (f & EPI_RAW) != 0;
+      n_act += (f & EPI_ACT) != 0;
+      n_res += (f & EPI_RESIDUAL) != 0;
+      const Seg& g = s.segs[i];
+      for (const Tensor* t : {&g.res, &g.raw, &g.actout})
+        if (t->p && (t->f32 || t->ld % 32 != 0)) return 0;
+      if (g.res_c0 % 32 || g.raw_c0 % 32 || g.act_c0 % 32) return 0;
+    }
+    if (n_raw > 1 || n_act > 1 || n_res > 1) return 0;
+    if (p.nseg == 2 && (n_res || p.seg[0].n1 % 32)) return 0;
+    if (n_act && s.N > PairCfg<256>::PARAM_COLS) return 0;
     for (int bn : {256, 192, 128})
       if (s.N % bn == 0) return bn;
     return 0;
@@ -543,11 +552,20 @@ struct Builder {
       }
       if (s.cin % 64 != 0) fail(KC_ERR_INVALID, "CUDA backend: GEMM input channels not padded");
       if (const int pbn = win ? 0 : pair_tile(s, p)) {
-        // the trunk's one-segment GEMMs: CTA-pair kernel with TMA-staged epilogue boxes
-        const Seg& g = s.segs[0];
-        const Tensor& out0 = g.raw.p ? g.raw : g.actout;
-        auto box = [&](const Tensor& t) { return make_box_map(t.p ? t.p : out0.p, bf16, t.p ? t.ld : out0.ld,
-                                                              rows_for(t.p ? t : out0)); };
+        // the trunk's GEMMs with one or two output segments: CTA-pair kernel with TMA-staged epilogue boxes; the
+        // raw, act and residual boxes each come from the (single) segment that has them
+        const Tensor *raw = nullptr, *act = nullptr, *res = nullptr;
+        p.pair_split = p.nseg > 1 ? p.seg[0].n1 : p.n_total;
+        for (int i = 0; i < p.nseg; i++) {
+          const Seg& g = s.segs[i];
+          const int n0 = p.seg[i].n0;
+          if (p.seg[i].flags & EPI_RAW) raw = &g.raw, p.pair_raw_x = g.raw_c0 - n0;
+          if (p.seg[i].flags & EPI_ACT) act = &g.actout, p.pair_act_x = g.act_c0 - n0;
+          if (p.seg[i].flags & EPI_RESIDUAL) res = &g.res, p.pair_res_x = g.res_c0 - n0;
+        }
+        const Tensor& out0 = raw ? *raw : *act;
+        auto box = [&](const Tensor* t) { return make_box_map(t ? t->p : out0.p, bf16, t ? t->ld : out0.ld,
+                                                              rows_for(t ? *t : out0)); };
         // 3x3 convolutions read one A window per 64-channel chunk (KATAGO_CUDA_PAIR_WIN=0: one A tile per tap)
         const char* pw = std::getenv("KATAGO_CUDA_PAIR_WIN");
         bool pwin = p.taps == PairCfg<256, true>::WIN_TAPS && !(pw && pw[0] == '0');
@@ -561,9 +579,9 @@ struct Builder {
         PairMaps pm;
         pm.a = make_map(s.A.p, bf16, s.A.ld, a_rows, pwin ? p.win_rows : 128);
         pm.b = make_map(dW, bf16, K, s.N, pbn / 2);
-        pm.res = box(g.res);
-        pm.raw = box(g.raw);
-        pm.act = box(g.actout);
+        pm.res = box(res);
+        pm.raw = box(raw);
+        pm.act = box(act);
         const int max_pairs = launch_pair<T>(true, pbn, pwin, 0, 0, pm, p);
         add(s.cls, [=](cudaStream_t st, int n) {
           GemmParams q = p;
@@ -677,33 +695,48 @@ struct Builder {
     const float* bi = up(bn.merged_bias);
     Engine::Impl* Ip = &I;
     const int Cw = y.ld;
+    if (xc0 % 8 != 0 || x.ld % 8 != 0 || Cw % 8 != 0)
+      fail(KC_ERR_INVALID, "CUDA backend: biased batch-norm pass on unaligned channels");
     add(CLS_OTHER, [=](cudaStream_t st, int n) {
-      int rows = n * 400;
-      size_t total = (size_t)rows * Cw;
-      bias_bnact_kernel<T><<<(unsigned)((total + 255) / 256), 256, 0, st>>>(
-          (const T*)x.p, x.ld, xc0, board_bias, sc, bi, act, Ip->rowmask, rows, C, Cw, (T*)y.p, y.ld);
+      const int rows = n * 400;
+      const unsigned blocks = (unsigned)(((size_t)rows * (Cw / 8) + 255) / 256);
+      auto go = [&](auto kernel) {
+        kernel<<<blocks, 256, 0, st>>>((const T*)x.p, x.ld, xc0, board_bias, sc, bi, Ip->rowmask, rows, C, Cw,
+                                       (T*)y.p, y.ld);
+      };
+      switch (act) {
+        case 1: go(bias_bnact_kernel<T, 1>); break;
+        case 2: go(bias_bnact_kernel<T, 2>); break;
+        case 3: go(bias_bnact_kernel<T, 3>); break;
+        default: go(bias_bnact_kernel<T, 0>); break;
+      }
     });
   }
   void pool(Tensor x, int c0, int C, bool value_mode, float* out) {
     Engine::Impl* Ip = &I;
+    const int CG = (C + 7) / 8;
+    if (CG > POOL_THREADS || c0 % 8 != 0 || x.ld % 8 != 0)
+      fail(KC_ERR_INVALID, "CUDA backend: pooled channels unaligned or too many");
+    const int smem = 2 * (POOL_THREADS / CG) * CG * 8 * (int)sizeof(float);
     add(CLS_OTHER, [=](cudaStream_t st, int n) {
-      dim3 grid(n, (C + 31) / 32);
-      pool_kernel<T><<<grid, dim3(32, 8), 0, st>>>((const T*)x.p, x.ld, c0, C, Ip->rowmask, Ip->mask_sum, Ip->scale1,
-                                                   Ip->scale2, value_mode ? 1 : 0, out);
+      pool_kernel<T><<<n, POOL_THREADS, smem, st>>>((const T*)x.p, x.ld, c0, C, Ip->rowmask, Ip->mask_sum,
+                                                    Ip->scale1, Ip->scale2, value_mode ? 1 : 0, out);
     });
   }
   void fc(const float* in, int in_ld, const MatMulDesc& mm, const MatBiasDesc* mb, Act act, float* out, int out_ld,
           int out_off, int out_stride) {
     const float* w = up(mm.w);
     const float* b = mb ? up(mb->b) : nullptr;
-    int ic = mm.ic, oc = mm.oc;
-    float** outp = nullptr;
-    (void)outp;
+    const int ic = mm.ic, oc = mm.oc;
+    const int smem = FC_BOARDS * ic * (int)sizeof(float);
+    if (smem > 227 * 1024) fail(KC_ERR_INVALID, "CUDA backend: head matmul input too wide");
+    if (smem > 48 * 1024) allow_smem(fc_kernel<FC_BOARDS>, smem);
     Engine::Impl* Ip = &I;
     const bool to_out = out == nullptr;  // null = the forward's output rows
     add(CLS_OTHER, [=](cudaStream_t st, int n) {
       float* o = to_out ? Ip->out : out;
-      fc_kernel<<<n, 128, ic * sizeof(float), st>>>(in, in_ld, ic, w, oc, b, act, o, out_ld, out_off, out_stride);
+      fc_kernel<FC_BOARDS><<<(n + FC_BOARDS - 1) / FC_BOARDS, 128, smem, st>>>(in, in_ld, ic, w, oc, b, act, o, out_ld, out_off,
+                                                                    out_stride, n);
     });
   }
   void rmsnorm(Tensor x, int C, const TfRmsDesc& d, Tensor y) {

@@ -89,6 +89,9 @@ struct alignas(16) GemmParams {
   // windowed A (tensor-core kernel with WIN): one window of win_rows rows starting halo rows above the tile
   int halo = 0, win_rows = 0;
   int win_base_mode = 1;  // descriptor base offset of a shifted window start: 0 = its 128 B row phase, 1 = zero
+  // CTA-pair kernel: columns >= pair_split belong to segment 1; the x coordinate of an output / residual box is
+  // pair_*_x + GEMM column (the segment's c0 minus its first column)
+  int pair_split = 0, pair_raw_x = 0, pair_act_x = 0, pair_res_x = 0;
   // SIMT kernel only
   const void* a = nullptr;
   int lda = 0;

@@ -199,11 +199,16 @@ __global__ void __launch_bounds__(PairCfg<BN, WIN>::THREADS, 1)
   static_assert((2 * C::STAGES + 9 + C::NRES * C::EPI_WARPS) * 8 + 8 <= C::BAR_BYTES, "barrier area");
   for (int i = threadIdx.x; i < (int)(sizeof(GemmParams) / 16); i += blockDim.x)
     reinterpret_cast<uint4*>(s_params)[i] = reinterpret_cast<const uint4*>(&p)[i];
-  const int flags = p.seg[0].flags;
+  // one or two column segments: [0, split) segment 0, [split, n_total) segment 1 (split a multiple of 32)
+  const int split = p.pair_split;
+  const int f0 = p.seg[0].flags, f1 = p.nseg > 1 ? p.seg[1].flags : f0;
+  const int flags = f0 | f1;
   if ((flags & EPI_ACT) && p.n_total <= C::PARAM_COLS) {
     for (int col = threadIdx.x; col < p.n_total; col += blockDim.x) {
-      s_scale[col] = p.seg[0].scale[col];
-      s_bias[col] = p.seg[0].bias[col];
+      const bool s1 = col >= split;
+      const bool act = ((s1 ? f1 : f0) & EPI_ACT) != 0;
+      s_scale[col] = act ? (s1 ? p.seg[1].scale[col - split] : p.seg[0].scale[col]) : 0.0f;
+      s_bias[col] = act ? (s1 ? p.seg[1].bias[col - split] : p.seg[0].bias[col]) : 0.0f;
     }
   }
 
@@ -425,9 +430,9 @@ __global__ void __launch_bounds__(PairCfg<BN, WIN>::THREADS, 1)
     uint8_t* st_raw = wbuf;
     uint8_t* st_act = wbuf + C::BOX_BYTES;
     uint64_t* rb = rbar + C::NRES * ew;
-    const bool has_res = (flags & EPI_RESIDUAL) != 0;
-    const int act = p.seg[0].act;
-    const int res_c0 = p.seg[0].res_c0, raw_c0 = p.seg[0].raw_c0, act_c0 = p.seg[0].act_c0;
+    const bool has_res = (flags & EPI_RESIDUAL) != 0;  // one-segment GEMMs only
+    const int a0 = p.seg[0].act, a1 = p.nseg > 1 ? p.seg[1].act : a0;
+    const int res_x = p.pair_res_x, raw_x = p.pair_raw_x, act_x = p.pair_act_x;
     const uint32_t tempty_leader0 = mapa_shared(smem_u32(&tempty[0]), 0);
 
     // residual boxes run NRES boxes ahead: box u (this warp's u-th 32-column chunk over its tiles) goes to buffer
@@ -439,7 +444,7 @@ __global__ void __launch_bounds__(PairCfg<BN, WIN>::THREADS, 1)
       const int mrow = (tile / n_tiles) * 256 + (int)rank * 128 + q * 32;
       const int col = (tile % n_tiles) * BN + h * C::WARP_COLS + c * 32;
       mbar_expect_tx(&rb[u % C::NRES], C::BOX_BYTES);
-      tma_load_2d(wbuf + (2 + u % C::NRES) * C::BOX_BYTES, &tmRes, &rb[u % C::NRES], res_c0 + col, mrow);
+      tma_load_2d(wbuf + (2 + u % C::NRES) * C::BOX_BYTES, &tmRes, &rb[u % C::NRES], res_x + col, mrow);
     };
     if (has_res && lane == 0)
       for (int i = 0; i < C::NRES; i++) res_issue(i);
@@ -498,16 +503,17 @@ __global__ void __launch_bounds__(PairCfg<BN, WIN>::THREADS, 1)
         // the previous box's stores must have read the staging boxes before they are overwritten
         if (lane == 0) bulk_wait_read0();
         __syncwarp();
-        if (flags & EPI_RAW) {
+        const int col = ncol0 + c * 32;
+        const int cf = col < split ? f0 : f1;  // this box's segment
+        if (cf & EPI_RAW) {
           float o[32];
 #pragma unroll
           for (int i = 0; i < 32; i++) o[i] = v[i] * m;
           stage_row<T>(st_raw, lane, o);
         }
-        if (flags & EPI_ACT) {
+        if (cf & EPI_ACT) {
           float o[32];
-          const int col = ncol0 + c * 32;
-          switch (act) {
+          switch (col < split ? a0 : a1) {
             case 1: pair_act<1>(v, s_scale + col, s_bias + col, m, o); break;
             case 2: pair_act<2>(v, s_scale + col, s_bias + col, m, o); break;
             case 3: pair_act<3>(v, s_scale + col, s_bias + col, m, o); break;
@@ -518,9 +524,8 @@ __global__ void __launch_bounds__(PairCfg<BN, WIN>::THREADS, 1)
         fence_proxy_async_smem();
         __syncwarp();
         if (lane == 0) {
-          const int col = ncol0 + c * 32;
-          if (flags & EPI_RAW) tma_store_2d(&tmRaw, st_raw, raw_c0 + col, mrow);
-          if (flags & EPI_ACT) tma_store_2d(&tmAct, st_act, act_c0 + col, mrow);
+          if (cf & EPI_RAW) tma_store_2d(&tmRaw, st_raw, raw_x + col, mrow);
+          if (cf & EPI_ACT) tma_store_2d(&tmAct, st_act, act_x + col, mrow);
           bulk_commit_group();
         }
       }

@@ -24,8 +24,13 @@ __global__ void prep_input_kernel(const float* __restrict__ in, int n, int cin, 
   int y = pos / 19, x = pos - y * 19;
   const float* src = in + (size_t)b * cin * 361 + pos;
   T* dst = out + ((size_t)b * brows + (size_t)(y + pad) * stride + x) * cpad;
-  for (int c = 0; c < cin; c++) dst[c] = from_f<T>(__ldg(src + (size_t)c * 361));
-  for (int c = cin; c < cpad; c++) dst[c] = from_f<T>(0.0f);
+  // cpad is a multiple of 8: the row is written as 16-byte vectors of 8 channels
+  for (int c0 = 0; c0 < cpad; c0 += 8) {
+    float v[8];
+#pragma unroll
+    for (int i = 0; i < 8; i++) v[i] = c0 + i < cin ? __ldg(src + (size_t)(c0 + i) * 361) : 0.0f;
+    store_vec<T, 8>(dst + c0, v);
+  }
   rowmask[pbl_row(b, y, x)] = __ldg(src);
 }
 
@@ -102,36 +107,58 @@ static __global__ void board_kernel(const __grid_constant__ BoardParams p) {
 // Masked pooling over a board's 361 points of channels [c0, c0 + C) of a PBL tensor (already masked):
 // gpool (bin2onnx.py :1222-1230): [mean, mean * scale1, max(x + (mask * 1e4 - 1e4))];
 // value (bin2onnx.py :1232-1239): [mean, mean * scale1, mean * scale2]. out [n][3C] float32.
-// grid (n, ceil(C / 32)), block (32, 8).
+// One block of POOL_THREADS per board: thread t takes the 8 channels (t % CG) * 8.. (CG = ceil(C / 8) groups) of
+// every RL-th point (RL = POOL_THREADS / CG row lanes), reading 16-byte vectors, then the row lanes are reduced in
+// shared memory ([RL][CG * 8] floats, twice). C is at most 8 * POOL_THREADS; c0 and the row pitch are multiples of 8
+// (the channels up to the next multiple of 8 are read and dropped).
 // ---------------------------------------------------------------------------------------------------------------
+constexpr int POOL_THREADS = 256;
 template <typename T>
-__global__ void pool_kernel(const T* __restrict__ x, int ld, int c0, int C, const float* __restrict__ rowmask,
-                            const float* __restrict__ mask_sum, const float* __restrict__ scale1,
-                            const float* __restrict__ scale2, int value_mode, float* __restrict__ out) {
-  __shared__ float ssum[8][32], smax[8][32];
+__global__ void __launch_bounds__(POOL_THREADS) pool_kernel(const T* __restrict__ x, int ld, int c0, int C,
+                                                            const float* __restrict__ rowmask,
+                                                            const float* __restrict__ mask_sum,
+                                                            const float* __restrict__ scale1,
+                                                            const float* __restrict__ scale2, int value_mode,
+                                                            float* __restrict__ out) {
+  extern __shared__ float pool_red[];  // [RL][Cp] sums, then [RL][Cp] maxima
   const int b = blockIdx.x;
-  const int c = blockIdx.y * 32 + threadIdx.x;
-  float s = 0.0f, mx = -INFINITY;
-  if (c < C) {
-    for (int pos = threadIdx.y; pos < 361; pos += 8) {
-      int y = pos / 19, xx = pos - y * 19;
-      int r = pbl_row(b, y, xx);
-      float v = to_f<T>(x[(size_t)r * ld + c0 + c]);
-      s += v;
-      float m = __ldg(rowmask + r);
-      float biasv = m * 1e4f - 1e4f;
-      mx = fmaxf(mx, v + biasv);
+  const int CG = (C + 7) >> 3, Cp = CG * 8, RL = POOL_THREADS / CG;
+  const int g = threadIdx.x % CG, rl = threadIdx.x / CG;
+  float* ssum = pool_red;
+  float* smax = pool_red + RL * Cp;
+  if (rl < RL) {
+    float s[8], mx[8];
+#pragma unroll
+    for (int i = 0; i < 8; i++) {
+      s[i] = 0.0f;
+      mx[i] = -INFINITY;
+    }
+    for (int pos = rl; pos < 361; pos += RL) {
+      const int y = pos / 19, xx = pos - y * 19;
+      const int r = pbl_row(b, y, xx);
+      float v[8];
+      load_vec<T, 8>(x + (size_t)r * ld + c0 + g * 8, v);
+      const float biasv = __ldg(rowmask + r) * 1e4f - 1e4f;
+#pragma unroll
+      for (int i = 0; i < 8; i++) {
+        s[i] += v[i];
+        mx[i] = fmaxf(mx[i], v[i] + biasv);
+      }
+    }
+#pragma unroll
+    for (int i = 0; i < 8; i++) {
+      ssum[rl * Cp + g * 8 + i] = s[i];
+      smax[rl * Cp + g * 8 + i] = mx[i];
     }
   }
-  ssum[threadIdx.y][threadIdx.x] = s;
-  smax[threadIdx.y][threadIdx.x] = mx;
   __syncthreads();
-  if (threadIdx.y == 0 && c < C) {
-    for (int i = 1; i < 8; i++) {
-      s += ssum[i][threadIdx.x];
-      mx = fmaxf(mx, smax[i][threadIdx.x]);
+  for (int c = threadIdx.x; c < C; c += POOL_THREADS) {
+    float s = 0.0f, mx = -INFINITY;
+    for (int i = 0; i < RL; i++) {
+      s += ssum[i * Cp + c];
+      mx = fmaxf(mx, smax[i * Cp + c]);
     }
-    float mean = s / mask_sum[b];
+    const float mean = s / mask_sum[b];
     float* o = out + (size_t)b * 3 * C;
     o[c] = mean;
     o[C + c] = mean * scale1[b];
@@ -141,20 +168,36 @@ __global__ void pool_kernel(const T* __restrict__ x, int ld, int c0, int C, cons
 
 // ---------------------------------------------------------------------------------------------------------------
 // Small per-board matmul: out[b][off + o * ostride] = act(sum_i in[b][i] * W[i][o] (+ bias[o])).
-// grid n, block 128.
+// NB boards per block, so that each weight read serves all of them. grid ceil(n / NB), block 128, shared memory
+// NB * ic floats.
 // ---------------------------------------------------------------------------------------------------------------
-static __global__ void fc_kernel(const float* __restrict__ in, int in_ld, int ic, const float* __restrict__ w, int oc,
-                          const float* __restrict__ bias, int act, float* __restrict__ out, int out_ld, int out_off,
-                          int out_stride) {
-  extern __shared__ float xin[];
-  const int b = blockIdx.x;
-  for (int i = threadIdx.x; i < ic; i += blockDim.x) xin[i] = in[(size_t)b * in_ld + i];
+constexpr int FC_BOARDS = 8;
+template <int NB>
+__global__ void fc_kernel(const float* __restrict__ in, int in_ld, int ic, const float* __restrict__ w, int oc,
+                                 const float* __restrict__ bias, int act, float* __restrict__ out, int out_ld,
+                                 int out_off, int out_stride, int n) {
+  extern __shared__ float xin[];  // [NB][ic]
+  const int b0 = blockIdx.x * NB;
+  const int nb = n - b0 < NB ? n - b0 : NB;
+  for (int i = threadIdx.x; i < NB * ic; i += blockDim.x) {
+    const int k = i / ic;
+    xin[i] = k < nb ? in[(size_t)(b0 + k) * in_ld + (i - k * ic)] : 0.0f;
+  }
   __syncthreads();
   for (int o = threadIdx.x; o < oc; o += blockDim.x) {
-    float a = 0.0f;
-    for (int i = 0; i < ic; i++) a += xin[i] * __ldg(w + (size_t)i * oc + o);
-    if (bias) a = a + bias[o];
-    out[(size_t)b * out_ld + out_off + (size_t)o * out_stride] = act_apply(a, act);
+    float a[NB];
+#pragma unroll
+    for (int k = 0; k < NB; k++) a[k] = 0.0f;
+    for (int i = 0; i < ic; i++) {
+      const float wv = __ldg(w + (size_t)i * oc + o);
+#pragma unroll
+      for (int k = 0; k < NB; k++) a[k] += xin[k * ic + i] * wv;
+    }
+    for (int k = 0; k < nb; k++) {
+      float v = a[k];
+      if (bias) v = v + bias[o];
+      out[(size_t)(b0 + k) * out_ld + out_off + (size_t)o * out_stride] = act_apply(v, act);
+    }
   }
 }
 
@@ -163,24 +206,42 @@ static __global__ void fc_kernel(const float* __restrict__ in, int in_ld, int ic
 // the gpool-biased regular branch (bin2onnx.py :1256-1258), the policy head's p1 (:1503-1504), and the standalone
 // bn_act_mask (:1170) where a producer could not fuse it. Rows [0, rows); y's channels [C, Cw) are written as 0.
 // ---------------------------------------------------------------------------------------------------------------
-template <typename T>
+// One thread per 8 channels of a row (16-byte loads and stores); the activation fixed at compile time. x's and y's
+// row pitches and xc0 are multiples of 8 elements, Cw a multiple of 8.
+template <typename T, int ACT>
 __global__ void bias_bnact_kernel(const T* __restrict__ x, int xld, int xc0, const float* __restrict__ board_bias,
-                                  const float* __restrict__ scale, const float* __restrict__ bias, int act,
+                                  const float* __restrict__ scale, const float* __restrict__ bias,
                                   const float* __restrict__ rowmask, int rows, int C, int Cw, T* __restrict__ y,
                                   int yld) {
-  size_t idx = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
-  if (idx >= (size_t)rows * Cw) return;
-  int r = (int)(idx / Cw), c = (int)(idx - (size_t)r * Cw);
-  float m = rowmask[r];
-  float o = 0.0f;
+  const int per_row = Cw >> 3;
+  const int idx = blockIdx.x * blockDim.x + threadIdx.x;
+  if (idx >= rows * per_row) return;
+  const int r = idx / per_row;
+  const int c = (idx - r * per_row) << 3;
+  const float m = __ldg(rowmask + r);
+  float o[8];
   if (c < C && m != 0.0f) {
-    float v = to_f<T>(x[(size_t)r * xld + xc0 + c]);
-    if (board_bias) v = v + board_bias[(size_t)(r / 400) * C + c];
-    float t = v * scale[c];
-    t = t + bias[c];
-    o = act_apply(t, act) * m;
+    float v[8];
+    load_vec<T, 8>(x + (size_t)r * xld + xc0 + c, v);
+    const float* bb = board_bias ? board_bias + (size_t)(r / 400) * C : nullptr;
+#pragma unroll
+    for (int i = 0; i < 8; i++) {
+      const int cc = c + i;
+      if (cc < C) {
+        float t = v[i];
+        if (bb) t = t + __ldg(bb + cc);
+        t = t * __ldg(scale + cc);
+        t = t + __ldg(bias + cc);
+        o[i] = act_fn<ACT>(t) * m;
+      } else {
+        o[i] = 0.0f;
+      }
+    }
+  } else {
+#pragma unroll
+    for (int i = 0; i < 8; i++) o[i] = 0.0f;
   }
-  y[(size_t)r * yld + c] = from_f<T>(o);
+  store_vec<T, 8>(y + (size_t)r * yld + c, o);
 }
 
 // ---------------------------------------------------------------------------------------------------------------

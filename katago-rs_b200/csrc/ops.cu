@@ -57,7 +57,7 @@ void launch_gpool_fc(const float* x, const float* mask, int n, int c, const floa
                      float* pooled, cudaStream_t st) {
   gpool_nchw_kernel<<<dim3(n, (c + 7) / 8), dim3(32, 8), 0, st>>>(x, mask, n, c, pooled);
   KC_CUDA(cudaGetLastError());
-  fc_kernel<<<n, 128, 3 * c * sizeof(float), st>>>(pooled, 3 * c, 3 * c, w, oc, nullptr, 0, out, oc, 0, 1);
+  fc_kernel<1><<<n, 128, 3 * c * sizeof(float), st>>>(pooled, 3 * c, 3 * c, w, oc, nullptr, 0, out, oc, 0, 1, n);
   KC_CUDA(cudaGetLastError());
 }
 
