@@ -35,11 +35,18 @@ struct PairCfg {
   static constexpr int WIN_MAX_ROWS = 176;        // 128 rows + a halo of up to 24 rows on each side
   static constexpr int A_WIN_BYTES = WIN_MAX_ROWS * 128;
   static constexpr int A_RING_BYTES = WIN ? 2 * A_WIN_BYTES : 0;
-  static constexpr int EPI_WARPS = 8;             // two per TMEM lane quarter, splitting the tile's columns
-  static constexpr int WARP_COLS = BN / 2;
+  // Epilogue warps: 2 or (1x1 tiles of BN = 192, whose time is the epilogue's) 3 per TMEM lane quarter, splitting
+  // the tile's columns; the windowed 3x3 keeps 2 (its third weight stage is worth more). With 12 epilogue warps
+  // the CTA has 16 (512 threads, 128 registers each at launch) and setmaxnreg moves registers from warpgroup 0
+  // (TMA producer, MMA issuer, two idle warps: 56 each) to the three epilogue warpgroups (152 each):
+  // 4 x 32 x 56 + 12 x 32 x 152 = 65,536, and per SMSP 56 + 3 x 152 = 512 x 32 = 16,384.
+  static constexpr int EPI_WARPS = BN == 192 && !WIN ? 12 : 8;
+  static constexpr int EPI_WARP0 = EPI_WARPS == 12 ? 4 : 2;  // first epilogue warp (a warpgroup boundary with 12)
+  static constexpr int WG0_REGS = 56, EPI_REGS = 152;
+  static constexpr int WARP_COLS = BN / (EPI_WARPS / 4);
   static constexpr int CHUNKS = WARP_COLS / 32;   // 32-column boxes per warp and tile
   static constexpr int BOX_BYTES = 32 * 32 * 2;   // 32 rows x 32 columns of a 2-byte type (64-byte swizzle)
-  static constexpr int NRES = WIN || BN > 192 ? 2 : 4;  // residual boxes in flight per epilogue warp (as fits)
+  static constexpr int NRES = WIN || BN > 128 ? 2 : 4;  // residual boxes in flight per epilogue warp (as fits)
   static constexpr int EPI_WARP_BYTES = (2 + NRES) * BOX_BYTES;  // raw box, act box, residual ring
   static constexpr int EPI_BYTES = EPI_WARPS * EPI_WARP_BYTES;
   static constexpr int PARAM_COLS = 768;          // per-column BN scale / bias in shared memory
@@ -55,7 +62,8 @@ struct PairCfg {
   static constexpr int SMEM = FIXED + STAGES * STAGE_BYTES;
   static constexpr uint32_t ACC_COLS = BN <= 64 ? 64 : BN <= 128 ? 128 : 256;
   static constexpr uint32_t TMEM_COLS = 2 * ACC_COLS;
-  static constexpr int THREADS = 64 + 32 * EPI_WARPS;
+  static constexpr int THREADS = 32 * (EPI_WARP0 + EPI_WARPS);
+  static_assert(WARP_COLS % 32 == 0, "epilogue warp columns");
 };
 
 // The 16-byte chunk `j` (0..3) of row `r` of a 32 x 64-byte box written by TMA with CU_TENSOR_MAP_SWIZZLE_64B:
@@ -199,8 +207,9 @@ __global__ void __launch_bounds__(PairCfg<BN, WIN>::THREADS, 1)
   static_assert((2 * C::STAGES + 9 + C::NRES * C::EPI_WARPS) * 8 + 8 <= C::BAR_BYTES, "barrier area");
   for (int i = threadIdx.x; i < (int)(sizeof(GemmParams) / 16); i += blockDim.x)
     reinterpret_cast<uint4*>(s_params)[i] = reinterpret_cast<const uint4*>(&p)[i];
-  // one or two column segments: [0, split) segment 0, [split, n_total) segment 1 (split a multiple of 32)
-  const int split = p.pair_split;
+  // one or two column segments: [0, split) segment 0, [split, n_total) segment 1 (split a multiple of 32); a
+  // one-segment GEMM never reads segment 1
+  const int split = p.nseg > 1 ? p.pair_split : p.n_total;
   const int f0 = p.seg[0].flags, f1 = p.nseg > 1 ? p.seg[1].flags : f0;
   const int flags = f0 | f1;
   if ((flags & EPI_ACT) && p.n_total <= C::PARAM_COLS) {
@@ -252,6 +261,8 @@ __global__ void __launch_bounds__(PairCfg<BN, WIN>::THREADS, 1)
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
 
+  if (warp < C::EPI_WARP0) {
+  if constexpr (C::EPI_WARPS == 12) asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(C::WG0_REGS));
   if (warp == 0) {
     if (lane == 0) {
       // ---- TMA producer (both CTAs): this CTA's A rows and half of B; the bytes count on the leader's barrier
@@ -421,9 +432,11 @@ __global__ void __launch_bounds__(PairCfg<BN, WIN>::THREADS, 1)
       }
     }
     __syncwarp();
+  }  // warps 2 .. EPI_WARP0 - 1: idle
   } else {
-    // ---- epilogue warps 2..9 (both CTAs): TMEM lane quarter warp % 4, column half (warp - 2) / 4
-    const int ew = warp - 2;
+    if constexpr (C::EPI_WARPS == 12) asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(C::EPI_REGS));
+    // ---- epilogue warps (both CTAs): TMEM lane quarter warp % 4, column part (warp - EPI_WARP0) / 4
+    const int ew = warp - C::EPI_WARP0;
     const int q = warp & 3;
     const int h = ew >> 2;
     uint8_t* wbuf = epi + ew * C::EPI_WARP_BYTES;
