@@ -19,8 +19,10 @@
 namespace kc {
 
 // WIN (3x3 convolutions, 9 taps): per 64-channel chunk, each CTA loads one A window (its 128 rows plus the taps'
-// halo above and below) into a ring of two, and every tap's MMA reads its 128 rows at the tap's row offset inside
-// the window; the pipeline stages then carry only weight boxes (three taps per stage: 12 MMAs per wait). This cuts the TMA bytes of a
+// halo above and below) into one of two window slots, and every tap's MMA reads its 128 rows at the tap's row offset
+// inside the window; the pipeline stages carry the weight boxes (three taps per stage: 12 MMAs per wait). The
+// window travels with its chunk's first stage, on that stage's barrier: no barriers of its own. Slot ch % 2 is free
+// when that stage's slot is (its MMAs follow chunk ch - 2's whenever STAGES <= 4, with 3 stages per chunk). This cuts the TMA bytes of a
 // 3x3 convolution's K-block from 28 KB to about 14 KB per CTA, below what TMA delivers per SM.
 template <int BN, bool WIN = false>
 struct PairCfg {
@@ -58,7 +60,7 @@ struct PairCfg {
       1024 /*align slack*/ + A_RING_BYTES + EPI_BYTES + PARAM_BYTES + PCOPY_BYTES + BAR_BYTES;
   static constexpr int FIT = (SMEM_LIMIT - FIXED) / STAGE_BYTES;
   static constexpr int STAGES = FIT > 4 ? 4 : FIT;
-  static_assert(STAGES >= 2, "pair pipeline depth");
+  static_assert(STAGES >= 2 && (!WIN || STAGES <= 4), "pair pipeline depth");
   static constexpr int SMEM = FIXED + STAGES * STAGE_BYTES;
   static constexpr uint32_t ACC_COLS = BN <= 64 ? 64 : BN <= 128 ? 128 : 256;
   static constexpr uint32_t TMEM_COLS = 2 * ACC_COLS;
@@ -198,13 +200,11 @@ __global__ void __launch_bounds__(PairCfg<BN, WIN>::THREADS, 1)
   uint64_t* tempty = tfull + 2;
   uint64_t* drain = tempty + 2;
   uint64_t* rbar = drain + 1;  // [EPI_WARPS][NRES]: the residual boxes of each epilogue warp
-  uint64_t* afull = rbar + C::NRES * C::EPI_WARPS;  // WIN: A window ring
-  uint64_t* aempty = afull + 2;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(aempty + 2);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(rbar + C::NRES * C::EPI_WARPS);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   static_assert(sizeof(GemmParams) <= C::PCOPY_BYTES && sizeof(GemmParams) % 16 == 0, "parameter copy");
-  static_assert((2 * C::STAGES + 9 + C::NRES * C::EPI_WARPS) * 8 + 8 <= C::BAR_BYTES, "barrier area");
+  static_assert((2 * C::STAGES + 5 + C::NRES * C::EPI_WARPS) * 8 + 8 <= C::BAR_BYTES, "barrier area");
   for (int i = threadIdx.x; i < (int)(sizeof(GemmParams) / 16); i += blockDim.x)
     reinterpret_cast<uint4*>(s_params)[i] = reinterpret_cast<const uint4*>(&p)[i];
   // one or two column segments: [0, split) segment 0, [split, n_total) segment 1 (split a multiple of 32); a
@@ -242,10 +242,6 @@ __global__ void __launch_bounds__(PairCfg<BN, WIN>::THREADS, 1)
     }
     mbar_init(drain, 1);
     for (int i = 0; i < C::NRES * C::EPI_WARPS; i++) mbar_init(&rbar[i], 1);
-    for (int a = 0; a < 2; a++) {
-      mbar_init(&afull[a], 1);
-      mbar_init(&aempty[a], 1);
-    }
     *abort_flag = 0;
     fence_mbar_init();
     prefetch_tensormap(&tmA);
@@ -270,7 +266,6 @@ __global__ void __launch_bounds__(PairCfg<BN, WIN>::THREADS, 1)
       uint32_t phase = 0;
       bool ok = true;
       int as = 0;
-      uint32_t aph = 0;
       // wait for a ring slot this CTA may refill; false (and abort) on a timeout
       auto slot_free = [&](uint64_t* bar, uint32_t parity) {
         if (mbar_try_wait(bar, parity)) return true;
@@ -283,18 +278,15 @@ __global__ void __launch_bounds__(PairCfg<BN, WIN>::THREADS, 1)
         const int nb = (tile % n_tiles) * BN + (int)rank * C::BH;
         if constexpr (WIN) {
           for (int ch = 0; ch < kb_per_tap && ok; ch++) {
-            if (!(ok = slot_free(&aempty[as], aph ^ 1))) break;
-            if (leader) mbar_expect_tx(&afull[as], 2u * (uint32_t)p.win_rows * 128u);
-            tma_load_2d_pair(awin + as * C::A_WIN_BYTES, &tmA, mapa_shared(smem_u32(&afull[as]), 0), ch * 64,
-                             m0 - p.halo);
-            if (++as == 2) {
-              as = 0;
-              aph ^= 1;
-            }
             for (int t0 = 0; t0 < C::WIN_TAPS; t0 += C::KBS) {
               if (!(ok = slot_free(&empty[stage], phase ^ 1))) break;
-              if (leader) mbar_expect_tx(&full[stage], 2u * C::KBS * C::B_BYTES);
+              const uint32_t win_bytes = t0 == 0 ? (uint32_t)p.win_rows * 128u : 0u;
+              if (leader) mbar_expect_tx(&full[stage], 2u * (C::KBS * C::B_BYTES + win_bytes));
               const uint32_t fb = mapa_shared(smem_u32(&full[stage]), 0);
+              if (t0 == 0) {  // the chunk's A window rides on its first stage
+                tma_load_2d_pair(awin + as * C::A_WIN_BYTES, &tmA, fb, ch * 64, m0 - p.halo);
+                as ^= 1;
+              }
               for (int j = 0; j < C::KBS; j++)
                 tma_load_2d_pair(stages + stage * C::STAGE_BYTES + j * C::KB_BYTES, &tmB, fb,
                                  (t0 + j) * p.cin + ch * 64, nb);
@@ -341,7 +333,6 @@ __global__ void __launch_bounds__(PairCfg<BN, WIN>::THREADS, 1)
       int stage = 0;
       uint32_t phase = 0;
       int as = 0;
-      uint32_t aph = 0;
       int local = 0;
       bool ok = true;
       // WIN: byte offset of each tap's 128 rows inside the window (halo + tap row offset; any row works: the
@@ -371,8 +362,8 @@ __global__ void __launch_bounds__(PairCfg<BN, WIN>::THREADS, 1)
         };
         if constexpr (WIN) {
           for (int ch = 0; ch < kb_per_tap && ok; ch++) {
-            if (!(ok = data_ready(&afull[as], aph))) break;
             const uint32_t swin = smem_u32(awin + as * C::A_WIN_BYTES);
+            as ^= 1;
 #pragma unroll
             for (int g = 0; g < C::WIN_TAPS / C::KBS; g++) {
               if (!(ok = data_ready(&full[stage], phase))) break;
@@ -394,11 +385,6 @@ __global__ void __launch_bounds__(PairCfg<BN, WIN>::THREADS, 1)
               }
             }
             if (!ok) break;
-            release(&aempty[as]);
-            if (++as == 2) {
-              as = 0;
-              aph ^= 1;
-            }
           }
         } else {
           for (int st = 0; st < NST; st++) {
