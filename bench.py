@@ -87,18 +87,57 @@ def peaks():
 
 
 class ClockSampler:
-    """nvidia-smi clocks and throttle reasons sampled every 200 ms during the timed region."""
+    """SM clocks and clock-event (throttle) reasons sampled every 10 ms during the timed region, through NVML
+    (read-only queries); nvidia-smi at its 200 ms period when NVML is unavailable."""
 
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    # NVML clock-event reason bits (nvml.h): SwPowerCap 0x4, HwSlowdown 0x8, SwThermalSlowdown 0x20,
+    # HwThermalSlowdown 0x40
+    REASON_BITS = {"sw_power_cap": 0x4, "hw_slowdown": 0x8, "sw_thermal_slowdown": 0x20, "hw_thermal_slowdown": 0x40}
 
-    def __init__(self, gpu_index):
+    def __init__(self, gpu_index, torch_device=None):
         self.gpu = gpu_index
+        self.dev = torch_device
         self.proc = None
+        self.thread = None
         self.path = os.path.join("/tmp", f"kc_clocks_{os.getpid()}.csv")
 
+    def _nvml_handle(self):
+        import pynvml
+        pynvml.nvmlInit()
+        if self.dev is not None:
+            try:
+                import torch
+                uuid = str(torch.cuda.get_device_properties(self.dev).uuid)
+                return pynvml, pynvml.nvmlDeviceGetHandleByUUID(uuid if uuid.startswith("GPU-") else "GPU-" + uuid)
+            except Exception:
+                pass
+        return pynvml, pynvml.nvmlDeviceGetHandleByIndex(self.gpu)
+
     def start(self):
+        import threading
+        try:
+            nv, h = self._nvml_handle()
+            self.samples = []
+            self.stop_evt = threading.Event()
+            max_mhz = nv.nvmlDeviceGetMaxClockInfo(h, nv.NVML_CLOCK_SM)
+
+            def run():
+                while not self.stop_evt.is_set():
+                    try:
+                        self.samples.append((nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM), max_mhz,
+                                             nv.nvmlDeviceGetCurrentClocksEventReasons(h)))
+                    except Exception:
+                        pass
+                    self.stop_evt.wait(0.01)
+
+            self.thread = threading.Thread(target=run, daemon=True)
+            self.thread.start()
+            return
+        except Exception:
+            self.thread = None
         try:
             self.fh = open(self.path, "w")
             self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
@@ -107,6 +146,15 @@ class ClockSampler:
             self.proc = None
 
     def stop(self):
+        if self.thread is not None:
+            self.stop_evt.set()
+            self.thread.join(timeout=5)
+            if not self.samples:
+                return None
+            reasons = sorted({nm for _, _, r in self.samples for nm, bit in self.REASON_BITS.items() if r & bit})
+            return {"sm_mhz": statistics.median(s[0] for s in self.samples),
+                    "sm_max_mhz": max(s[1] for s in self.samples), "reasons": reasons,
+                    "samples": len(self.samples), "source": "nvml, 10 ms"}
         if self.proc is None:
             return None
         self.proc.terminate()
@@ -132,7 +180,7 @@ class ClockSampler:
         if not sm:
             return None
         return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(mx), "reasons": sorted(reasons),
-                "samples": len(sm)}
+                "samples": len(sm), "source": "nvidia-smi, 200 ms"}
 
 
 def cpu_baseline(args, seconds, threads=0):
@@ -255,7 +303,7 @@ def run_ours(args):
     if dist:
         dist.barrier()
     torch.cuda.synchronize()
-    clocks = ClockSampler(local)
+    clocks = ClockSampler(local, dev)
     clocks.start()
     # headline: the plain graph; then the same K steps again with an event pair around every launch, which gives
     # the per-kernel-class device times (the events cost a few percent, so they stay out of the headline)
