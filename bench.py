@@ -31,10 +31,17 @@ REPO = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, os.path.join(REPO, "katago-rs_b200", "python"))
 
 METRIC = "b18c384nbt evals/s at batch 256 per GPU"
+
+
+def metric_name(args):
+    """The headline metric, or the same metric for another --net / --batch (a parity or exploration run)."""
+    if args.net == "b18c384nbt" and args.batch == 256:
+        return METRIC
+    return f"{args.net} evals/s at batch {args.batch} per GPU"
 UNIT = "evals/s"
 # DRAM bytes (read + write) per 3x3-convolution GEMM launch at batch 256, from the full ncu capture summarised in
 # profiles/gemm_pair_b18c384nbt_batch256.md (mean of the two 3x3 launches captured).
-CONV3_DRAM_BYTES_PER_LAUNCH = 74.8e6
+CONV3_DRAM_BYTES_PER_LAUNCH = 75.0e6
 
 
 def parse():
@@ -225,7 +232,7 @@ def run_reference(args):
     value = per * args.steps / tot
     cores = os.cpu_count()
     line = {
-        "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": args.gpus, "steps": args.steps,
+        "impl": "reference", "metric": metric_name(args), "value": value, "unit": UNIT, "n_gpus": args.gpus, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": 1e3 * tot / args.steps, "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "f32", "data": "synthetic",
         "config": {"workload": f"{args.net} forward, {per} boards per step of the batch-{args.batch} workload "
@@ -353,7 +360,7 @@ def run_ours(args):
         other = {k: {"ms_per_step": v[0] / args.steps, "launches_per_step": v[1] / args.steps}
                  for k, v in prof.items()}
         line = {
-            "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+            "metric": metric_name(args), "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": max_ms / args.steps, "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": args.precision, "data": "synthetic",
             "config": {"workload": f"{args.net} forward pass, batch {args.batch} per GPU, {args.precision} "
