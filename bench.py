@@ -210,6 +210,15 @@ def cpu_baseline(args, seconds, threads=0):
     return done / el, done, el
 
 
+def host_threads():
+    """The host threads this process may use (its CPU affinity set). Passed to the oracle's OpenMP explicitly:
+    torchrun sets OMP_NUM_THREADS=1 for every rank."""
+    try:
+        return len(os.sched_getaffinity(0))
+    except AttributeError:
+        return os.cpu_count() or 1
+
+
 def run_reference(args):
     rank, world, _ = dist_env()
     if rank != 0:
@@ -220,17 +229,17 @@ def run_reference(args):
     net = OracleNet(netgen.net_bytes(args.net))
     spatial, glob, _, _ = workload(args, 0)
     per = 4
+    cores = host_threads()
     for i in range(args.warmup):
-        net.forward(spatial[:per], glob[:per])
+        net.forward(spatial[:per], glob[:per], threads=cores)
     times = []
     for i in range(args.steps):
         j = (i * per) % (args.batch - per + 1)
         t0 = time.perf_counter()
-        net.forward(spatial[j:j + per], glob[j:j + per])
+        net.forward(spatial[j:j + per], glob[j:j + per], threads=cores)
         times.append(time.perf_counter() - t0)
     tot = sum(times)
     value = per * args.steps / tot
-    cores = os.cpu_count()
     line = {
         "impl": "reference", "metric": metric_name(args), "value": value, "unit": UNIT, "n_gpus": args.gpus, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": 1e3 * tot / args.steps, "higher_is_better": True, "scaling": "weak",
@@ -384,8 +393,8 @@ def run_ours(args):
             "clocks": clk,
         }
         if world == 1 and not args.no_cpu_baseline:
-            v, n, el = cpu_baseline(args, args.cpu_seconds)
-            line["cpu_baseline"] = {"value": v, "unit": UNIT, "cores": os.cpu_count(), "kind": "port",
+            v, n, el = cpu_baseline(args, args.cpu_seconds, threads=host_threads())
+            line["cpu_baseline"] = {"value": v, "unit": UNIT, "cores": host_threads(), "kind": "port",
                                     "sample": f"{n} boards of the batch-{args.batch} workload in {el:.1f} s, "
                                               "CPU oracle float32 (reference arithmetic restated in C++), "
                                               "OpenMP on all host threads"}
