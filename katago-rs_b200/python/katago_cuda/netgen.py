@@ -192,6 +192,13 @@ def small_nbt() -> NetSpec:
     return NetSpec("small-nbt", 14, 384, blocks, stem_k=5, act=ACT_MISH, v2=80)
 
 
+def wide_nbt() -> NetSpec:
+    """256-channel trunk: the CTA-pair GEMM's 256-wide tiles (windowed 3x3, the gpool conv's two segments
+    192 + 64, the 1x1 post conv with a residual) and 128-wide tiles (the nested block's 1x1 pre conv and 3x3)."""
+    blocks: List[Block] = [Ordinary(), GPool(regular=192, gpool=64), _nested(128, [Ordinary()])]
+    return NetSpec("wide-nbt", 14, 256, blocks, stem_k=3, act=ACT_MISH, v2=48)
+
+
 def small_tf() -> NetSpec:
     """b10c384h6's shapes with 2 blocks."""
     blocks: List[Block] = []
@@ -213,6 +220,7 @@ NETS = {
     "tiny-tf-spatial": tiny_tf_spatial,
     "small-nbt": small_nbt,
     "small-tf": small_tf,
+    "wide-nbt": wide_nbt,
 }
 
 
