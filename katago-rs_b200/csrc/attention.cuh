@@ -64,6 +64,8 @@ template <typename T>
 __global__ void __launch_bounds__(AttnCfg::THREADS, 1)
     attention_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                         const __grid_constant__ CUtensorMap tmV, const __grid_constant__ AttnParams p) {
+  pdl_wait();
+  pdl_trigger();
   using C = AttnCfg;
   constexpr int fmt = std::is_same<T, __nv_bfloat16>::value ? 1 : 0;
   constexpr uint32_t IDESC_S = make_idesc_f16(fmt, 128, 208);

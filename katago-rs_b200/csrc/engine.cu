@@ -95,6 +95,33 @@ void allow_smem(K* kernel, int bytes) {
   done.insert(key);
 }
 
+// Programmatic dependent launch: every kernel of a forward pass is launched with programmatic stream
+// serialization, so that it can start (and run its prologue) on SMs the previous kernel has left; each kernel
+// waits (griddepcontrol.wait) before its first access to memory an earlier kernel writes. KATAGO_CUDA_PDL=0 turns
+// it off.
+bool pdl_enabled() {
+  static const bool on = [] {
+    const char* e = std::getenv("KATAGO_CUDA_PDL");
+    return !(e && e[0] == '0');
+  }();
+  return on;
+}
+
+template <typename... KArgs, typename... Args>
+void launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st, Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  at[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cfg.attrs = at;
+  cfg.numAttrs = pdl_enabled() ? 1 : 0;
+  KC_CUDA(cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...));
+}
+
 template <typename T, int BN, bool RF32, bool WIN>
 void launch_tc_bn(bool prepare, int grid, cudaStream_t s, const CUtensorMap& a, const CUtensorMap& b,
                   const GemmParams& p) {
@@ -103,7 +130,7 @@ void launch_tc_bn(bool prepare, int grid, cudaStream_t s, const CUtensorMap& a, 
     allow_smem(gemm_tc_kernel<T, BN, RF32, WIN>, C::SMEM);
     return;
   }
-  gemm_tc_kernel<T, BN, RF32, WIN><<<grid, C::THREADS, C::SMEM, s>>>(a, b, p);
+  launch_pdl(gemm_tc_kernel<T, BN, RF32, WIN>, dim3(grid), dim3(C::THREADS), C::SMEM, s, a, b, p);
 }
 
 template <typename T, bool RF32, bool WIN>
@@ -167,6 +194,11 @@ int launch_pair_bn(bool prepare, int pairs, cudaStream_t s, const PairMaps& m, c
     if (clusters <= 0) fail(KC_ERR_CUDA, "CUDA backend: no CTA pair of the trunk GEMM fits on this device");
     return clusters;
   }
+  cudaLaunchAttribute at2[2] = {at[0], {}};
+  at2[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  at2[1].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = at2;
+  cfg.numAttrs = pdl_enabled() ? 2 : 1;
   cfg.gridDim = dim3(2 * pairs);
   KC_CUDA(cudaLaunchKernelEx(&cfg, gemm_pair_kernel<T, BN, WIN>, m.a, m.b, m.res, m.raw, m.act, p));
   return pairs;
@@ -614,7 +646,7 @@ struct Builder {
         GemmParams q = p;
         q.g.rows = n * brows;
         dim3 grid((q.g.rows + 63) / 64, (q.n_total + 63) / 64);
-        gemm_simt_kernel<T><<<grid, 256, 0, st>>>(q);
+        launch_pdl(gemm_simt_kernel<T>, dim3(grid), dim3(256), 0, st, q);
       });
     }
   }
@@ -701,7 +733,7 @@ struct Builder {
       const int rows = n * 400;
       const unsigned blocks = (unsigned)(((size_t)rows * (Cw / 8) + 255) / 256);
       auto go = [&](auto kernel) {
-        kernel<<<blocks, 256, 0, st>>>((const T*)x.p, x.ld, xc0, board_bias, sc, bi, Ip->rowmask, rows, C, Cw,
+        launch_pdl(kernel, dim3(blocks), dim3(256), 0, st, (const T*)x.p, x.ld, xc0, board_bias, sc, bi, Ip->rowmask, rows, C, Cw,
                                        (T*)y.p, y.ld);
       };
       switch (act) {
@@ -719,7 +751,7 @@ struct Builder {
       fail(KC_ERR_INVALID, "CUDA backend: pooled channels unaligned or too many");
     const int smem = 2 * (POOL_THREADS / CG) * CG * 8 * (int)sizeof(float);
     add(CLS_OTHER, [=](cudaStream_t st, int n) {
-      pool_kernel<T><<<n, POOL_THREADS, smem, st>>>((const T*)x.p, x.ld, c0, C, Ip->rowmask, Ip->mask_sum,
+      launch_pdl(pool_kernel<T>, dim3(n), dim3(POOL_THREADS), smem, st, (const T*)x.p, x.ld, c0, C, Ip->rowmask, Ip->mask_sum,
                                                     Ip->scale1, Ip->scale2, value_mode ? 1 : 0, out);
     });
   }
@@ -735,7 +767,7 @@ struct Builder {
     const bool to_out = out == nullptr;  // null = the forward's output rows
     add(CLS_OTHER, [=](cudaStream_t st, int n) {
       float* o = to_out ? Ip->out : out;
-      fc_kernel<FC_BOARDS><<<(n + FC_BOARDS - 1) / FC_BOARDS, 128, smem, st>>>(in, in_ld, ic, w, oc, b, act, o, out_ld, out_off,
+      launch_pdl(fc_kernel<FC_BOARDS>, dim3((n + FC_BOARDS - 1) / FC_BOARDS), dim3(128), smem, st, in, in_ld, ic, w, oc, b, act, o, out_ld, out_off,
                                                                     out_stride, n);
     });
   }
@@ -746,10 +778,10 @@ struct Builder {
     add(CLS_OTHER, [=](cudaStream_t st, int n) {
       int rows = n * 400;
       if (x.f32)
-        rmsnorm_kernel<float, T><<<(rows + 7) / 8, 256, 0, st>>>((const float*)x.p, x.ld, C, w, eps, Ip->rowmask, rows,
+        launch_pdl(rmsnorm_kernel<float, T>, dim3((rows + 7) / 8), dim3(256), 0, st, (const float*)x.p, x.ld, C, w, eps, Ip->rowmask, rows,
                                                                 (T*)y.p, y.ld);
       else
-        rmsnorm_kernel<T, T><<<(rows + 7) / 8, 256, 0, st>>>((const T*)x.p, x.ld, C, w, eps, Ip->rowmask, rows,
+        launch_pdl(rmsnorm_kernel<T, T>, dim3((rows + 7) / 8), dim3(256), 0, st, (const T*)x.p, x.ld, C, w, eps, Ip->rowmask, rows,
                                                             (T*)y.p, y.ld);
     });
   }
@@ -880,7 +912,7 @@ struct Builder {
       add(CLS_OTHER, [=](cudaStream_t st, int n) {
         int rows = n * 400;
         size_t total = (size_t)rows * ((qc + kc) / 2);
-        rope_kernel<T><<<(unsigned)((total + 255) / 256), 256, 0, st>>>((T*)QKV.p, QKV.ld, qc, kc, hd, dcos, dsin,
+        launch_pdl(rope_kernel<T>, dim3((unsigned)((total + 255) / 256)), dim3(256), 0, st, (T*)QKV.p, QKV.ld, qc, kc, hd, dcos, dsin,
                                                                         tstride, group, rows);
       });
     }
@@ -906,7 +938,7 @@ struct Builder {
           ap.err = I.d_err;
           allow_smem(attention_tc_kernel<T>, AttnCfg::SMEM);
           add(CLS_ATTN, [=](cudaStream_t st, int n) {
-            attention_tc_kernel<T><<<dim3(4, nh, n), AttnCfg::THREADS, AttnCfg::SMEM, st>>>(tq, tk, tv, ap);
+            launch_pdl(attention_tc_kernel<T>, dim3(dim3(4, nh, n)), dim3(AttnCfg::THREADS), AttnCfg::SMEM, st, tq, tk, tv, ap);
           });
         }
         Spec so;
@@ -955,7 +987,7 @@ struct Builder {
   template <int HD>
   static void launch_attn(dim3 grid, size_t smem, cudaStream_t st, Tensor QKV, int qc, int kc, int nh, int nkv,
                           float scale, const float* rowmask, Tensor O) {
-    attention_simt_kernel<T, HD><<<grid, 128, smem, st>>>((const T*)QKV.p, QKV.ld, qc, kc, nh, nkv, scale, rowmask,
+    launch_pdl(attention_simt_kernel<T, HD>, dim3(grid), dim3(128), smem, st, (const T*)QKV.p, QKV.ld, qc, kc, nh, nkv, scale, rowmask,
                                                          (T*)O.p, O.ld);
   }
 
@@ -995,7 +1027,7 @@ struct Builder {
       add(CLS_OTHER, [=](cudaStream_t st, int n) {
         int rows = n * 400;
         size_t total = (size_t)rows * F;
-        swiglu_kernel<T><<<(unsigned)((total + 255) / 256), 256, 0, st>>>((const T*)AG.p, AG.ld, F, Ip->rowmask, rows,
+        launch_pdl(swiglu_kernel<T>, dim3((unsigned)((total + 255) / 256)), dim3(256), 0, st, (const T*)AG.p, AG.ld, F, Ip->rowmask, rows,
                                                                          (T*)H.p, H.ld);
       });
     }
@@ -1032,7 +1064,7 @@ struct Builder {
       const int cin = m.num_input_channels, cpad = stem_cin, brows = stem_brows, stride = stem_stride, pad = stem_pad;
       Engine::Impl* Ip = &I;
       add(CLS_OTHER, [=](cudaStream_t st, int n) {
-        prep_input_kernel<T><<<(n * 361 + 127) / 128, 128, 0, st>>>(Ip->in_spatial, n, cin, (T*)STEM.p, STEM.ld, brows,
+        launch_pdl(prep_input_kernel<T>, dim3((n * 361 + 127) / 128), dim3(128), 0, st, Ip->in_spatial, n, cin, (T*)STEM.p, STEM.ld, brows,
                                                                     stride, pad, Ip->rowmask);
       });
       (void)cpad;
@@ -1058,7 +1090,7 @@ struct Builder {
         q.spatial = Ip->in_spatial;
         q.glob = Ip->in_global;
         q.meta = meta ? Ip->in_meta : nullptr;
-        board_kernel<<<n, 256, 0, st>>>(q);
+        launch_pdl(board_kernel, dim3(n), dim3(256), 0, st, q);
       });
     }
     // stem conv + per-board bias -> X (remapped into the PBL), XA = first block's pre-BN act
@@ -1109,10 +1141,10 @@ struct Builder {
       Engine::Impl* Ip = &I;
       add(CLS_OTHER, [=](cudaStream_t st, int n) {
         if (X.f32)
-          tip_rms_kernel<float, T><<<n, 512, 0, st>>>((const float*)X.p, X.ld, C, g, bb, eps, spatial, act,
+          launch_pdl(tip_rms_kernel<float, T>, dim3(n), dim3(512), 0, st, (const float*)X.p, X.ld, C, g, bb, eps, spatial, act,
                                                       Ip->rowmask, Ip->mask_sum, (T*)XA.p, XA.ld);
         else
-          tip_rms_kernel<T, T><<<n, 512, 0, st>>>((const T*)X.p, X.ld, C, g, bb, eps, spatial, act, Ip->rowmask,
+          launch_pdl(tip_rms_kernel<T, T>, dim3(n), dim3(512), 0, st, (const T*)X.p, X.ld, C, g, bb, eps, spatial, act, Ip->rowmask,
                                                   Ip->mask_sum, (T*)XA.p, XA.ld);
       });
     }
@@ -1150,7 +1182,7 @@ struct Builder {
       const int v1c0 = P1p + G1p;
       Engine::Impl* Ip = &I;
       add(CLS_OTHER, [=](cudaStream_t st, int n) {
-        head_spatial_kernel<T><<<(n * 361 + 127) / 128, 128, 0, st>>>((const T*)P1A.p, P1A.ld, p1c, w2, P,
+        launch_pdl(head_spatial_kernel<T>, dim3((n * 361 + 127) / 128), dim3(128), 0, st, (const T*)P1A.p, P1A.ld, p1c, w2, P,
                                                                      (const T*)HEAD.p, HEAD.ld, v1c0, v1c, wo, Ip->out,
                                                                      row_len, own_off, n);
       });

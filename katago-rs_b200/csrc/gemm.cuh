@@ -570,6 +570,9 @@ __global__ void __launch_bounds__(TcCfg<BN, WIN>::THREADS, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  // everything above (barriers, TMEM, parameter and BN-table copies) overlaps the previous kernel's tail
+  pdl_wait();
+  pdl_trigger();
 
   if (warp == 0) {
     if (lane == 0) {
@@ -779,6 +782,8 @@ __global__ void __launch_bounds__(TcCfg<BN, WIN>::THREADS, 1)
 
 template <typename T>
 __global__ void __launch_bounds__(256) gemm_simt_kernel(const __grid_constant__ GemmParams p) {
+  pdl_wait();
+  pdl_trigger();
   static_assert(sizeof(T) == 4, "the SIMT GEMM is the float32 path");
   __shared__ float As[16][64 + 4];
   __shared__ float Ws[16][64 + 4];

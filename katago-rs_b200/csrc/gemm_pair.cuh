@@ -256,6 +256,10 @@ __global__ void __launch_bounds__(PairCfg<BN, WIN>::THREADS, 1)
   cluster_sync();  // both CTAs' barriers exist before any cross-CTA arrive or transaction
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  // everything above (barriers, TMEM, cluster barrier, parameter and BN-table copies) overlaps the previous
+  // kernel's tail
+  pdl_wait();
+  pdl_trigger();
 
   if (warp < C::EPI_WARP0) {
   if constexpr (C::EPI_WARPS == 12) asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(C::WG0_REGS));

@@ -18,6 +18,8 @@ __host__ __device__ __forceinline__ int pbl_row(int b, int y, int x) { return b 
 template <typename T>
 __global__ void prep_input_kernel(const float* __restrict__ in, int n, int cin, T* __restrict__ out, int cpad,
                                   int brows, int stride, int pad, float* __restrict__ rowmask) {
+  pdl_wait();
+  pdl_trigger();
   int idx = blockIdx.x * blockDim.x + threadIdx.x;
   if (idx >= n * 361) return;
   int b = idx / 361, pos = idx - b * 361;
@@ -56,6 +58,8 @@ struct BoardParams {
 };
 
 static __global__ void board_kernel(const __grid_constant__ BoardParams p) {
+  pdl_wait();
+  pdl_trigger();
   __shared__ float red[256];
   __shared__ float hbuf[2][512];
   const int b = blockIdx.x;
@@ -120,6 +124,8 @@ __global__ void __launch_bounds__(POOL_THREADS) pool_kernel(const T* __restrict_
                                                             const float* __restrict__ scale1,
                                                             const float* __restrict__ scale2, int value_mode,
                                                             float* __restrict__ out) {
+  pdl_wait();
+  pdl_trigger();
   extern __shared__ float pool_red[];  // [RL][Cp] sums, then [RL][Cp] maxima
   const int b = blockIdx.x;
   const int CG = (C + 7) >> 3, Cp = CG * 8, RL = POOL_THREADS / CG;
@@ -176,6 +182,8 @@ template <int NB>
 __global__ void fc_kernel(const float* __restrict__ in, int in_ld, int ic, const float* __restrict__ w, int oc,
                                  const float* __restrict__ bias, int act, float* __restrict__ out, int out_ld,
                                  int out_off, int out_stride, int n) {
+  pdl_wait();
+  pdl_trigger();
   extern __shared__ float xin[];  // [NB][ic]
   const int b0 = blockIdx.x * NB;
   const int nb = n - b0 < NB ? n - b0 : NB;
@@ -213,6 +221,8 @@ __global__ void bias_bnact_kernel(const T* __restrict__ x, int xld, int xc0, con
                                   const float* __restrict__ scale, const float* __restrict__ bias,
                                   const float* __restrict__ rowmask, int rows, int C, int Cw, T* __restrict__ y,
                                   int yld) {
+  pdl_wait();
+  pdl_trigger();
   const int per_row = Cw >> 3;
   const int idx = blockIdx.x * blockDim.x + threadIdx.x;
   if (idx >= rows * per_row) return;
@@ -251,6 +261,8 @@ __global__ void bias_bnact_kernel(const T* __restrict__ x, int xld, int xc0, con
 template <typename TI, typename T>
 __global__ void rmsnorm_kernel(const TI* __restrict__ x, int ld, int C, const float* __restrict__ w, float eps,
                                const float* __restrict__ rowmask, int rows, T* __restrict__ y, int yld) {
+  pdl_wait();
+  pdl_trigger();
   int r = blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
   int lane = threadIdx.x & 31;
   if (r >= rows) return;
@@ -278,6 +290,8 @@ __global__ void tip_rms_kernel(const TI* __restrict__ x, int ld, int C, const fl
                                const float* __restrict__ beta, float eps, int spatial, int act,
                                const float* __restrict__ rowmask, const float* __restrict__ mask_sum,
                                T* __restrict__ y, int yld) {
+  pdl_wait();
+  pdl_trigger();
   __shared__ float rms_s[361];
   __shared__ float red[32];
   const int b = blockIdx.x;
@@ -339,6 +353,8 @@ __global__ void head_spatial_kernel(const T* __restrict__ p1a, int p1ld, int p1c
                                     int P, const T* __restrict__ v1a, int v1ld, int v1c0, int v1c,
                                     const float* __restrict__ wown, float* __restrict__ out, int row_len, int own_off,
                                     int n) {
+  pdl_wait();
+  pdl_trigger();
   int idx = blockIdx.x * blockDim.x + threadIdx.x;
   if (idx >= n * 361) return;
   int b = idx / 361, pos = idx - b * 361;
@@ -362,6 +378,8 @@ __global__ void head_spatial_kernel(const T* __restrict__ p1a, int p1ld, int p1c
 template <typename T>
 __global__ void rope_kernel(T* __restrict__ qkv, int ld, int qc, int kc, int hd, const float* __restrict__ cosv,
                             const float* __restrict__ sinv, int table_stride, int group, int rows) {
+  pdl_wait();
+  pdl_trigger();
   const int half = hd / 2;
   const int pairs_per_row = (qc + kc) / 2;
   size_t idx = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
@@ -386,6 +404,8 @@ __global__ void rope_kernel(T* __restrict__ qkv, int ld, int qc, int kc, int hd,
 template <typename T>
 __global__ void swiglu_kernel(const T* __restrict__ ag, int ld, int F, const float* __restrict__ rowmask, int rows,
                               T* __restrict__ h, int hld) {
+  pdl_wait();
+  pdl_trigger();
   size_t idx = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (idx >= (size_t)rows * F) return;
   int r = (int)(idx / F), j = (int)(idx - (size_t)r * F);
@@ -406,6 +426,8 @@ __global__ void __launch_bounds__(128) attention_simt_kernel(const T* __restrict
                                                              int heads, int kv_heads, float scale,
                                                              const float* __restrict__ rowmask, T* __restrict__ out,
                                                              int out_ld) {
+  pdl_wait();
+  pdl_trigger();
   extern __shared__ uint8_t sm[];
   T* Ks = reinterpret_cast<T*>(sm);
   T* Vs = Ks + 361 * HD;

@@ -202,6 +202,13 @@ __host__ __device__ constexpr uint32_t make_idesc_f16(int fmt, int m, int n) {
          | ((uint32_t)(m >> 4) << 24);    // M / 16
 }
 
+// ---- programmatic dependent launch ----
+// A kernel launched with programmatic stream serialization may start while the previous kernel in the stream is
+// still running: it waits here, before its first access to memory that kernel writes (a no-op without the launch
+// attribute). Triggering lets the next kernel in the stream start its own prologue on SMs this one leaves idle.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
 // ---- CTA pairs (clusters of 2) and tcgen05 with cta_group::2 ----
 
 __device__ __forceinline__ uint32_t cluster_ctarank() {
