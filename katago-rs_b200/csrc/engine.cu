@@ -767,7 +767,7 @@ struct Builder {
     const bool to_out = out == nullptr;  // null = the forward's output rows
     add(CLS_OTHER, [=](cudaStream_t st, int n) {
       float* o = to_out ? Ip->out : out;
-      launch_pdl(fc_kernel<FC_BOARDS>, dim3((n + FC_BOARDS - 1) / FC_BOARDS), dim3(128), smem, st, in, in_ld, ic, w, oc, b, act, o, out_ld, out_off,
+      launch_pdl(fc_kernel<FC_BOARDS>, dim3((n + FC_BOARDS - 1) / FC_BOARDS, (oc + 31) / 32), dim3(FC_THREADS), smem, st, in, in_ld, ic, w, oc, b, act, o, out_ld, out_off,
                                                                     out_stride, n);
     });
   }

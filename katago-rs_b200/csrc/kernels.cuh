@@ -174,17 +174,22 @@ __global__ void __launch_bounds__(POOL_THREADS) pool_kernel(const T* __restrict_
 
 // ---------------------------------------------------------------------------------------------------------------
 // Small per-board matmul: out[b][off + o * ostride] = act(sum_i in[b][i] * W[i][o] (+ bias[o])).
-// NB boards per block, so that each weight read serves all of them. grid ceil(n / NB), block 128, shared memory
-// NB * ic floats.
+// A block computes 32 outputs (blockIdx.y) for NB boards (blockIdx.x): its 8 warps split the input dimension,
+// lane = output (coalesced weight rows), and the 8 partial sums are added in shared memory. grid (ceil(n / NB),
+// ceil(oc / 32)), block FC_THREADS, shared memory NB * ic floats (the boards' inputs).
 // ---------------------------------------------------------------------------------------------------------------
-constexpr int FC_BOARDS = 8;
+constexpr int FC_BOARDS = 4;
+constexpr int FC_THREADS = 256;
 template <int NB>
-__global__ void fc_kernel(const float* __restrict__ in, int in_ld, int ic, const float* __restrict__ w, int oc,
-                                 const float* __restrict__ bias, int act, float* __restrict__ out, int out_ld,
-                                 int out_off, int out_stride, int n) {
+__global__ void __launch_bounds__(FC_THREADS) fc_kernel(const float* __restrict__ in, int in_ld, int ic,
+                                                        const float* __restrict__ w, int oc,
+                                                        const float* __restrict__ bias, int act,
+                                                        float* __restrict__ out, int out_ld, int out_off,
+                                                        int out_stride, int n) {
   pdl_wait();
   pdl_trigger();
   extern __shared__ float xin[];  // [NB][ic]
+  __shared__ float part[FC_THREADS / 32][NB][32];
   const int b0 = blockIdx.x * NB;
   const int nb = n - b0 < NB ? n - b0 : NB;
   for (int i = threadIdx.x; i < NB * ic; i += blockDim.x) {
@@ -192,19 +197,33 @@ __global__ void fc_kernel(const float* __restrict__ in, int in_ld, int ic, const
     xin[i] = k < nb ? in[(size_t)(b0 + k) * in_ld + (i - k * ic)] : 0.0f;
   }
   __syncthreads();
-  for (int o = threadIdx.x; o < oc; o += blockDim.x) {
-    float a[NB];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int o = blockIdx.y * 32 + lane;
+  constexpr int NW = FC_THREADS / 32;
+  const int i0 = (int)((long long)ic * warp / NW), i1 = (int)((long long)ic * (warp + 1) / NW);
+  float a[NB];
 #pragma unroll
-    for (int k = 0; k < NB; k++) a[k] = 0.0f;
-    for (int i = 0; i < ic; i++) {
+  for (int k = 0; k < NB; k++) a[k] = 0.0f;
+  if (o < oc) {
+#pragma unroll 4
+    for (int i = i0; i < i1; i++) {
       const float wv = __ldg(w + (size_t)i * oc + o);
 #pragma unroll
       for (int k = 0; k < NB; k++) a[k] += xin[k * ic + i] * wv;
     }
-    for (int k = 0; k < nb; k++) {
-      float v = a[k];
-      if (bias) v = v + bias[o];
-      out[(size_t)(b0 + k) * out_ld + out_off + (size_t)o * out_stride] = act_apply(v, act);
+  }
+#pragma unroll
+  for (int k = 0; k < NB; k++) part[warp][k][lane] = a[k];
+  __syncthreads();
+  if (threadIdx.x < NB * 32) {
+    const int k = threadIdx.x >> 5;
+    const int oo = blockIdx.y * 32 + (threadIdx.x & 31);
+    if (k < nb && oo < oc) {
+      float v = 0.0f;
+#pragma unroll
+      for (int j = 0; j < NW; j++) v += part[j][k][threadIdx.x & 31];
+      if (bias) v = v + bias[oo];
+      out[(size_t)(b0 + k) * out_ld + out_off + (size_t)oo * out_stride] = act_apply(v, act);
     }
   }
 }
@@ -234,17 +253,33 @@ __global__ void bias_bnact_kernel(const T* __restrict__ x, int xld, int xc0, con
     float v[8];
     load_vec<T, 8>(x + (size_t)r * xld + xc0 + c, v);
     const float* bb = board_bias ? board_bias + (size_t)(r / 400) * C : nullptr;
+    if (c + 8 <= C && (C & 3) == 0) {
+      // whole vector inside the channels: parameters as 16-byte loads
+      float sc[8], bi[8], bv[8];
+      load_vec<float, 8>(scale + c, sc);
+      load_vec<float, 8>(bias + c, bi);
+      if (bb) load_vec<float, 8>(bb + c, bv);
 #pragma unroll
-    for (int i = 0; i < 8; i++) {
-      const int cc = c + i;
-      if (cc < C) {
+      for (int i = 0; i < 8; i++) {
         float t = v[i];
-        if (bb) t = t + __ldg(bb + cc);
-        t = t * __ldg(scale + cc);
-        t = t + __ldg(bias + cc);
+        if (bb) t = t + bv[i];
+        t = t * sc[i];
+        t = t + bi[i];
         o[i] = act_fn<ACT>(t) * m;
-      } else {
-        o[i] = 0.0f;
+      }
+    } else {
+#pragma unroll
+      for (int i = 0; i < 8; i++) {
+        const int cc = c + i;
+        if (cc < C) {
+          float t = v[i];
+          if (bb) t = t + __ldg(bb + cc);
+          t = t * __ldg(scale + cc);
+          t = t + __ldg(bias + cc);
+          o[i] = act_fn<ACT>(t) * m;
+        } else {
+          o[i] = 0.0f;
+        }
       }
     }
   } else {

@@ -6,6 +6,7 @@
 #include <cuda_runtime.h>
 
 #include <mutex>
+#include <set>
 #include <string>
 
 #include "../../include/katago_cuda.h"
@@ -52,12 +53,27 @@ void check_gpool_args(const float* x, const float* mask, int n, int c, const flo
   if (3 * c > 12 * 1024) fail(KC_ERR_INVALID, "CUDA backend: gpool: 3 * channels above 12288");
 }
 
+// fc_kernel<1> with up to 3 * 4096 input floats: above the 48 KB of shared memory a kernel gets without opting in
+// (its inputs plus its static reduction buffer). Once per device; not a stream operation.
+void allow_fc_smem() {
+  static std::mutex mu;
+  static std::set<int> done;
+  int dev = 0;
+  KC_CUDA(cudaGetDevice(&dev));
+  std::lock_guard<std::mutex> lock(mu);
+  if (done.count(dev)) return;
+  KC_CUDA(cudaFuncSetAttribute(fc_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, 12 * 1024 * sizeof(float)));
+  done.insert(dev);
+}
+
 // pooled (scratch [n][3c]) -> out = pooled x w ([3c][oc]), both launched on `st`.
 void launch_gpool_fc(const float* x, const float* mask, int n, int c, const float* w, int oc, float* out,
                      float* pooled, cudaStream_t st) {
   gpool_nchw_kernel<<<dim3(n, (c + 7) / 8), dim3(32, 8), 0, st>>>(x, mask, n, c, pooled);
   KC_CUDA(cudaGetLastError());
-  fc_kernel<1><<<n, 128, 3 * c * sizeof(float), st>>>(pooled, 3 * c, 3 * c, w, oc, nullptr, 0, out, oc, 0, 1, n);
+  allow_fc_smem();
+  fc_kernel<1><<<dim3(n, (oc + 31) / 32), FC_THREADS, 3 * c * sizeof(float), st>>>(pooled, 3 * c, 3 * c, w, oc,
+                                                                              nullptr, 0, out, oc, 0, 1, n);
   KC_CUDA(cudaGetLastError());
 }
 
