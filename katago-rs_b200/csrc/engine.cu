@@ -412,12 +412,15 @@ struct Builder {
 
   // ---- weights ----
   // W [N][taps * cin_pad]: conv (file order [ky][kx][ic][oc]) at output rows [n_off, n_off + oc)
+  // W[n_off + o][tap * cin_pad + i] = conv weight (tap = ky * kx_n + kx); cin_pad 0 packs the taps densely
+  // (tap * ic + i, the stem's im2col operand)
   static void pack_conv(std::vector<float>& W, int K, int cin_pad, int n_off, const ConvDesc& c) {
+    const int stride = cin_pad ? cin_pad : c.ic;
     for (int ky = 0; ky < c.ky; ky++)
       for (int kx = 0; kx < c.kx; kx++)
         for (int i = 0; i < c.ic; i++)
           for (int o = 0; o < c.oc; o++)
-            W[(size_t)(n_off + o) * K + (ky * c.kx + kx) * cin_pad + i] =
+            W[(size_t)(n_off + o) * K + (ky * c.kx + kx) * stride + i] =
                 c.w[(((size_t)ky * c.kx + kx) * c.ic + i) * c.oc + o];
   }
   static void pack_linear(std::vector<float>& W, int K, int n_off, const MatMulDesc& mm, const int* perm = nullptr,
@@ -457,8 +460,8 @@ struct Builder {
   };
 
   // Tile width of the CTA-pair kernel for this GEMM, or 0 when the one-CTA kernel must run it: one or two column
-  // segments of 2-byte raw / batch-norm-activation outputs (a 2-byte residual only with one segment), each kind of
-  // output in at most one segment, on 32-column-aligned operands. KATAGO_CUDA_PAIR=0 sends every GEMM to the
+  // segments of 2-byte raw / batch-norm-activation outputs (a 2-byte residual or a per-board bias only with one
+  // segment), each kind of output in at most one segment, on 32-column-aligned operands. KATAGO_CUDA_PAIR=0 sends every GEMM to the
   // one-CTA kernel.
   int pair_tile(const Spec& s, const GemmParams& p) const {
     const char* e = std::getenv("KATAGO_CUDA_PAIR");
@@ -467,7 +470,9 @@ struct Builder {
     int n_raw = 0, n_act = 0, n_res = 0;
     for (int i = 0; i < p.nseg; i++) {
       const int f = p.seg[i].flags;
-      if ((f & ~(EPI_RAW | EPI_ACT | EPI_RESIDUAL)) || !(f & (EPI_RAW | EPI_ACT))) return 0;
+      if ((f & ~(EPI_RAW | EPI_ACT | EPI_RESIDUAL | EPI_BOARD_BIAS)) || !(f & (EPI_RAW | EPI_ACT))) return 0;
+      // per-board bias: one segment, 16-byte aligned rows (the stem)
+      if ((f & EPI_BOARD_BIAS) && (p.nseg != 1 || p.seg[i].ld_bb % 4 != 0)) return 0;
       n_raw += (f & EPI_RAW) != 0;
       n_act += (f & EPI_ACT) != 0;
       n_res += (f & EPI_RESIDUAL) != 0;
@@ -1056,18 +1061,30 @@ struct Builder {
     stem_brows = (19 + stem_pad) * stem_stride;
     stem_cin = round_up(m.num_input_channels, tc ? 64 : 16);
     I.stem_rows = round_up(max_batch * stem_brows, 128) + 2 * (stem_pad * stem_stride + stem_pad) + 128;
+    // tensor-core tiers: the stem reads an im2col operand in the PBL (one tap, K = taps x planes padded to 64)
+    const bool im2col = tc && round_up(stem_k * stem_k * m.num_input_channels, 64) <= IM2COL_MAX_K;
+    const int stem_dil = std::max(ic.dy, 1);
+    if (im2col) {
+      stem_cin = round_up(stem_k * stem_k * m.num_input_channels, 64);
+      I.stem_rows = round_up(max_batch * 400, 128) + 128;
+    }
 
     Tensor X = tensor(R_LEVEL0, C), XA = tensor(R_LEVEL0 + 1, C);
     Tensor STEM = tensor(R_STEM, stem_cin);
     // stem input layout + per-board statistics and trunk bias
     {
-      const int cin = m.num_input_channels, cpad = stem_cin, brows = stem_brows, stride = stem_stride, pad = stem_pad;
+      const int cin = m.num_input_channels, brows = stem_brows, stride = stem_stride, pad = stem_pad;
       Engine::Impl* Ip = &I;
+      const int sk = stem_k;
       add(CLS_OTHER, [=](cudaStream_t st, int n) {
-        launch_pdl(prep_input_kernel<T>, dim3((n * 361 + 127) / 128), dim3(128), 0, st, Ip->in_spatial, n, cin, (T*)STEM.p, STEM.ld, brows,
-                                                                    stride, pad, Ip->rowmask);
+        if (im2col)
+          launch_pdl(prep_im2col_kernel<T>, dim3((n * 400 + IM2COL_ROWS - 1) / IM2COL_ROWS), dim3(256),
+                     (size_t)IM2COL_ROWS * (STEM.ld + 8) * sizeof(T), st, Ip->in_spatial, n, cin, sk, stem_dil, (T*)STEM.p,
+                     STEM.ld, Ip->rowmask);
+        else
+          launch_pdl(prep_input_kernel<T>, dim3((n * 361 + 127) / 128), dim3(128), 0, st, Ip->in_spatial, n, cin,
+                     (T*)STEM.p, STEM.ld, brows, stride, pad, Ip->rowmask);
       });
-      (void)cpad;
       BoardParams bp;
       std::memset(&bp, 0, sizeof(bp));
       bp.cin = cin;
@@ -1100,17 +1117,21 @@ struct Builder {
       s.cls = CLS_STEM;
       s.A = STEM;
       s.cin = stem_cin;
-      s.stem = true;
       s.taps.clear();
-      const int d = std::max(ic.dy, 1);
-      for (int ky = 0; ky < stem_k; ky++)
-        for (int kx = 0; kx < stem_k; kx++)
-          s.taps.push_back(((ky - stem_k / 2) * stem_stride + (kx - stem_k / 2)) * d);
+      if (im2col) {
+        s.taps.push_back(0);  // one tap over the im2col operand, ordinary PBL rows
+      } else {
+        s.stem = true;
+        for (int ky = 0; ky < stem_k; ky++)
+          for (int kx = 0; kx < stem_k; kx++)
+            s.taps.push_back(((ky - stem_k / 2) * stem_stride + (kx - stem_k / 2)) * stem_dil);
+      }
       s.N = w16(C);
       const int K = (int)s.taps.size() * s.cin;
       if (pass == 1) {
         s.W.assign((size_t)s.N * K, 0.0f);
-        pack_conv(s.W, K, s.cin, 0, ic);
+        // im2col column of (tap, plane) = tap * planes + plane; else tap * padded planes + plane
+        pack_conv(s.W, K, im2col ? 0 : s.cin, 0, ic);
       }
       Seg g;
       g.width = w16(C);

@@ -483,6 +483,18 @@ __global__ void __launch_bounds__(PairCfg<BN, WIN>::THREADS, 1)
         float v[32];
 #pragma unroll
         for (int i = 0; i < 32; i++) v[i] = __uint_as_float(x[i]);
+        if ((f0 & EPI_BOARD_BIAS) && m != 0.0f) {
+          // per-board bias (one-segment GEMMs: the stem's global-feature term), 32 columns of this row's board
+          const float* bb = p.seg[0].board_bias + (size_t)(r / 400) * p.seg[0].ld_bb + ncol0 + c * 32;
+#pragma unroll
+          for (int j = 0; j < 32; j += 4) {
+            const float4 q = __ldg(reinterpret_cast<const float4*>(bb + j));
+            v[j] += q.x;
+            v[j + 1] += q.y;
+            v[j + 2] += q.z;
+            v[j + 3] += q.w;
+          }
+        }
         if (has_res) {
           if (!mbar_wait(&rb[u % C::NRES], (u / C::NRES) & 1, p.err, DEV_TIMEOUT_EPILOGUE)) {
             *abort_flag = 1;

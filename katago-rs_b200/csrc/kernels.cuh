@@ -37,6 +37,79 @@ __global__ void prep_input_kernel(const float* __restrict__ in, int n, int cin, 
 }
 
 // ---------------------------------------------------------------------------------------------------------------
+// Input -> the stem's im2col operand (tensor-core tiers): row = PBL row of (b, y, x), column = tap * cin + c with
+// tap = ky * k + kx, value in[b][c][y + (ky - k/2) d][x + (kx - k/2) d] (0 off the 19 x 19 grid and on halo rows,
+// the stem conv's zero padding); columns [k * k * cin, kpad) are 0. Also the per-PBL-row on-board mask (input
+// channel 0, bin2onnx.py setup_mask :1203-1206). The stem then is a one-tap GEMM with K = kpad (576 for a 5x5 stem
+// over 22 planes) instead of 25 taps of 64 padded channels. kpad % 8 == 0, kpad <= IM2COL_MAX_K.
+// ---------------------------------------------------------------------------------------------------------------
+constexpr int IM2COL_ROWS = 32;
+constexpr int IM2COL_MAX_K = 704;  // kpad limit: tile (IM2COL_ROWS x (kpad + 8) x 2 bytes) + column table <= 48 KB
+template <typename T>
+__global__ void __launch_bounds__(256) prep_im2col_kernel(const float* __restrict__ in, int n, int cin, int k, int d,
+                                                          T* __restrict__ out, int kpad, float* __restrict__ rowmask) {
+  pdl_wait();
+  pdl_trigger();
+  // A block fills IM2COL_ROWS consecutive PBL rows: the gathers walk the rows (consecutive board points, so
+  // consecutive input addresses per plane), a shared-memory tile transposes, and the rows leave as 16-byte vectors.
+  extern __shared__ uint8_t im2col_raw[];
+  T* tile = reinterpret_cast<T*>(im2col_raw);  // [IM2COL_ROWS][kpad + 8]: rows 16 bytes apart from a bank multiple
+  const int ts = kpad + 8;
+  __shared__ int col_code[IM2COL_MAX_K];  // per column: plane << 16 | (dy + 128) << 8 | (dx + 128); -1 past k*k*cin
+  const int r0 = blockIdx.x * IM2COL_ROWS;
+  const int rows = n * 400;
+  const int kk = k * k * cin;
+  for (int j = threadIdx.x; j < kpad; j += blockDim.x) {
+    int code = -1;
+    if (j < kk) {
+      const int t = j / cin, c = j - t * cin;
+      const int ky = t / k, kx = t - ky * k;
+      code = (c << 16) | (((ky - k / 2) * d + 128) << 8) | ((kx - k / 2) * d + 128);
+    }
+    col_code[j] = code;
+  }
+  __syncthreads();
+  // thread t fills row t % IM2COL_ROWS (decoded once) at columns t / IM2COL_ROWS, + 8, ...: a warp walks 32
+  // consecutive rows of one column
+  const int i = threadIdx.x % IM2COL_ROWS;
+  const int r = r0 + i;
+  int b = 0, y = -1, x = 0;
+  if (r < rows) {
+    b = r / 400;
+    const int rr = r - b * 400;
+    y = rr / 20 - 1;
+    x = rr - (rr / 20) * 20;
+  }
+  const bool on = r < rows && y >= 0 && x < 19;
+  const float* src = in + (size_t)b * cin * 361;
+  for (int j = threadIdx.x / IM2COL_ROWS; j < kpad; j += blockDim.x / IM2COL_ROWS) {
+    const int code = col_code[j];
+    float val = 0.0f;
+    if (on && code >= 0) {
+      const int yy = y + ((code >> 8) & 255) - 128, xx = x + (code & 255) - 128;
+      if (yy >= 0 && yy < 19 && xx >= 0 && xx < 19) val = __ldg(src + (size_t)(code >> 16) * 361 + yy * 19 + xx);
+    }
+    tile[i * ts + j] = from_f<T>(val);
+  }
+  __syncthreads();
+  const int per_row = kpad >> 3;
+  for (int e = threadIdx.x; e < IM2COL_ROWS * per_row; e += blockDim.x) {
+    const int i = e / per_row, g = e - i * per_row;
+    const int r = r0 + i;
+    if (r < rows)
+      *reinterpret_cast<uint4*>(out + (size_t)r * kpad + g * 8) = *reinterpret_cast<const uint4*>(tile + i * ts + g * 8);
+  }
+  if (threadIdx.x < IM2COL_ROWS) {
+    const int r = r0 + threadIdx.x;
+    if (r < rows) {
+      const int b = r / 400, rr = r - b * 400;
+      const int y = rr / 20 - 1, x = rr - (rr / 20) * 20;
+      if (y >= 0 && x < 19) rowmask[r] = __ldg(in + (size_t)b * cin * 361 + y * 19 + x);
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------------------------------------------
 // Per board: mask sum and the pooling scales (bin2onnx.py setup_mask :1207-1215), and the trunk's per-board bias:
 // global features x initial matmul, plus the SGF-metadata encoder for human-SL nets (bin2onnx.py :1467-1487).
 // ---------------------------------------------------------------------------------------------------------------

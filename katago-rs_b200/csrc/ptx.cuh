@@ -167,14 +167,16 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
       : "memory");
 }
 
-// 16 consecutive floats from shared memory (16-byte aligned) as four 128-bit shared loads.
+// 16 consecutive floats from shared memory (16-byte aligned) as four 128-bit shared loads. Only for tables that
+// no thread writes after the kernel's prologue barrier: the loads are not volatile, so the compiler may hoist and
+// interleave them with the arithmetic.
 __device__ __forceinline__ void lds16(const float* p, float (&v)[16]) {
   const uint32_t a = smem_u32(p);
 #pragma unroll
   for (int j = 0; j < 4; j++)
-    asm volatile("ld.shared.v4.f32 {%0,%1,%2,%3}, [%4];"
-                 : "=f"(v[4 * j]), "=f"(v[4 * j + 1]), "=f"(v[4 * j + 2]), "=f"(v[4 * j + 3])
-                 : "r"(a + 16 * j));
+    asm("ld.shared.v4.f32 {%0,%1,%2,%3}, [%4];"
+        : "=f"(v[4 * j]), "=f"(v[4 * j + 1]), "=f"(v[4 * j + 2]), "=f"(v[4 * j + 3])
+        : "r"(a + 16 * j));
 }
 
 // Shared-memory matrix descriptor of a K-major tile stored as 128-byte rows with the 128B swizzle (the layout a
