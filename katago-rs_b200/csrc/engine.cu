@@ -342,7 +342,7 @@ enum Role : int {
   R_LEVEL0 = 16,  // + 2 * depth (+0 stream, +1 act)
   R_COUNT = 32
 };
-enum FRole : int { F_POOL, F_GBIAS, F_VPOOL, F_V2, F_PASS, F_COUNT };
+enum FRole : int { F_POOL, F_GBIAS, F_VPOOL, F_V2, F_PASS, F_PIX, F_COUNT };
 
 template <typename T>
 struct Builder {
@@ -1062,10 +1062,11 @@ struct Builder {
     stem_cin = round_up(m.num_input_channels, tc ? 64 : 16);
     I.stem_rows = round_up(max_batch * stem_brows, 128) + 2 * (stem_pad * stem_stride + stem_pad) + 128;
     // tensor-core tiers: the stem reads an im2col operand in the PBL (one tap, K = taps x planes padded to 64)
-    const bool im2col = tc && round_up(stem_k * stem_k * m.num_input_channels, 64) <= IM2COL_MAX_K;
+    const bool im2col = tc;
     const int stem_dil = std::max(ic.dy, 1);
+    const int pix_c = round_up(m.num_input_channels, 8);  // planes per pixel of the im2col staging grid
     if (im2col) {
-      stem_cin = round_up(stem_k * stem_k * m.num_input_channels, 64);
+      stem_cin = round_up(stem_k * stem_k * pix_c, 64);
       I.stem_rows = round_up(max_batch * 400, 128) + 128;
     }
 
@@ -1075,13 +1076,16 @@ struct Builder {
     {
       const int cin = m.num_input_channels, brows = stem_brows, stride = stem_stride, pad = stem_pad;
       Engine::Impl* Ip = &I;
-      const int sk = stem_k;
+      const int sk = stem_k, grid_px = (19 + 2 * pad) * (19 + 2 * pad);
+      // im2col staging: [n][G][G][pix_c] of T, as a per-board float buffer
+      T* pix = im2col ? reinterpret_cast<T*>(fbuffer(F_PIX, (grid_px * pix_c * (int)sizeof(T) + 3) / 4)) : nullptr;
       add(CLS_OTHER, [=](cudaStream_t st, int n) {
-        if (im2col)
-          launch_pdl(prep_im2col_kernel<T>, dim3((n * 400 + IM2COL_ROWS - 1) / IM2COL_ROWS), dim3(256),
-                     (size_t)IM2COL_ROWS * (STEM.ld + 8) * sizeof(T), st, Ip->in_spatial, n, cin, sk, stem_dil, (T*)STEM.p,
-                     STEM.ld, Ip->rowmask);
-        else
+        if (im2col) {
+          launch_pdl(prep_pixels_kernel<T>, dim3((n * grid_px + 255) / 256), dim3(256), 0, st, Ip->in_spatial, n, cin,
+                     pad, pix, pix_c, Ip->rowmask);
+          launch_pdl(prep_im2col_kernel<T>, dim3((n * 400 * (sk * sk + 1) + 255) / 256), dim3(256), 0, st,
+                     (const T*)pix, n, sk, stem_dil, pad, pix_c, (T*)STEM.p, STEM.ld);
+        } else
           launch_pdl(prep_input_kernel<T>, dim3((n * 361 + 127) / 128), dim3(128), 0, st, Ip->in_spatial, n, cin,
                      (T*)STEM.p, STEM.ld, brows, stride, pad, Ip->rowmask);
       });
@@ -1130,8 +1134,8 @@ struct Builder {
       const int K = (int)s.taps.size() * s.cin;
       if (pass == 1) {
         s.W.assign((size_t)s.N * K, 0.0f);
-        // im2col column of (tap, plane) = tap * planes + plane; else tap * padded planes + plane
-        pack_conv(s.W, K, im2col ? 0 : s.cin, 0, ic);
+        // im2col column of (tap, plane) = tap * planes padded to 8 + plane; else tap * padded planes + plane
+        pack_conv(s.W, K, im2col ? pix_c : s.cin, 0, ic);
       }
       Seg g;
       g.width = w16(C);

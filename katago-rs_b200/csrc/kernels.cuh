@@ -37,75 +37,64 @@ __global__ void prep_input_kernel(const float* __restrict__ in, int n, int cin, 
 }
 
 // ---------------------------------------------------------------------------------------------------------------
-// Input -> the stem's im2col operand (tensor-core tiers): row = PBL row of (b, y, x), column = tap * cin + c with
-// tap = ky * k + kx, value in[b][c][y + (ky - k/2) d][x + (kx - k/2) d] (0 off the 19 x 19 grid and on halo rows,
-// the stem conv's zero padding); columns [k * k * cin, kpad) are 0. Also the per-PBL-row on-board mask (input
-// channel 0, bin2onnx.py setup_mask :1203-1206). The stem then is a one-tap GEMM with K = kpad (576 for a 5x5 stem
-// over 22 planes) instead of 25 taps of 64 padded channels. kpad % 8 == 0, kpad <= IM2COL_MAX_K.
+// Input -> the stem's im2col operand (tensor-core tiers), in two steps.
+// prep_pixels_kernel: planes [n][cin][361] float32 -> pixel-major px [n][G][G][CP] (G = 19 + 2 pad, CP = cin
+// rounded up to 8; the pad-wide border and planes [cin, CP) zero), and the per-PBL-row on-board mask (input channel
+// 0, bin2onnx.py setup_mask :1203-1206). One thread per grid pixel.
+// prep_im2col_kernel: row = PBL row of (b, y, x), columns [tap * CP, tap * CP + CP) = px[b][y + ky d][x + kx d]
+// (tap = ky * k + kx; the border supplies the stem conv's zero padding), columns [k * k * CP, kpad) and halo rows
+// zero: K = kpad (640 for a 5x5 stem over 22 planes) instead of 25 taps of 64 padded channels. One thread per
+// (row, tap) copying CP / 8 16-byte vectors; tap k * k zeroes the tail.
 // ---------------------------------------------------------------------------------------------------------------
-constexpr int IM2COL_ROWS = 32;
-constexpr int IM2COL_MAX_K = 704;  // kpad limit: tile (IM2COL_ROWS x (kpad + 8) x 2 bytes) + column table <= 48 KB
 template <typename T>
-__global__ void __launch_bounds__(256) prep_im2col_kernel(const float* __restrict__ in, int n, int cin, int k, int d,
-                                                          T* __restrict__ out, int kpad, float* __restrict__ rowmask) {
+__global__ void prep_pixels_kernel(const float* __restrict__ in, int n, int cin, int pad, T* __restrict__ px, int cp,
+                                   float* __restrict__ rowmask) {
   pdl_wait();
   pdl_trigger();
-  // A block fills IM2COL_ROWS consecutive PBL rows: the gathers walk the rows (consecutive board points, so
-  // consecutive input addresses per plane), a shared-memory tile transposes, and the rows leave as 16-byte vectors.
-  extern __shared__ uint8_t im2col_raw[];
-  T* tile = reinterpret_cast<T*>(im2col_raw);  // [IM2COL_ROWS][kpad + 8]: rows 16 bytes apart from a bank multiple
-  const int ts = kpad + 8;
-  __shared__ int col_code[IM2COL_MAX_K];  // per column: plane << 16 | (dy + 128) << 8 | (dx + 128); -1 past k*k*cin
-  const int r0 = blockIdx.x * IM2COL_ROWS;
-  const int rows = n * 400;
-  const int kk = k * k * cin;
-  for (int j = threadIdx.x; j < kpad; j += blockDim.x) {
-    int code = -1;
-    if (j < kk) {
-      const int t = j / cin, c = j - t * cin;
+  const int G = 19 + 2 * pad;
+  const int idx = blockIdx.x * blockDim.x + threadIdx.x;
+  if (idx >= n * G * G) return;
+  const int b = idx / (G * G), q = idx - b * G * G;
+  const int gy = q / G, gx = q - gy * G;
+  const int y = gy - pad, x = gx - pad;
+  const bool on = y >= 0 && y < 19 && x >= 0 && x < 19;
+  const float* src = in + (size_t)b * cin * 361 + (on ? y * 19 + x : 0);
+  T* dst = px + (size_t)idx * cp;
+  for (int c0 = 0; c0 < cp; c0 += 8) {
+    float v[8];
+#pragma unroll
+    for (int i = 0; i < 8; i++) v[i] = on && c0 + i < cin ? __ldg(src + (size_t)(c0 + i) * 361) : 0.0f;
+    store_vec<T, 8>(dst + c0, v);
+  }
+  if (on) rowmask[pbl_row(b, y, x)] = __ldg(src);
+}
+
+template <typename T>
+__global__ void prep_im2col_kernel(const T* __restrict__ px, int n, int k, int d, int pad, int cp,
+                                   T* __restrict__ out, int kpad) {
+  pdl_wait();
+  pdl_trigger();
+  const int taps = k * k;
+  const int idx = blockIdx.x * blockDim.x + threadIdx.x;
+  if (idx >= n * 400 * (taps + 1)) return;
+  const int r = idx / (taps + 1), t = idx - r * (taps + 1);
+  const int b = r / 400, rr = r - b * 400;
+  const int y = rr / 20 - 1, x = rr - (rr / 20) * 20;
+  const bool on = y >= 0 && x < 19;
+  uint4* dst = reinterpret_cast<uint4*>(out + (size_t)r * kpad);
+  const int nv = cp >> 3;
+  if (t < taps) {
+    uint4* d0 = dst + t * nv;
+    if (on) {
       const int ky = t / k, kx = t - ky * k;
-      code = (c << 16) | (((ky - k / 2) * d + 128) << 8) | ((kx - k / 2) * d + 128);
+      const int G = 19 + 2 * pad;
+      const uint4* s = reinterpret_cast<const uint4*>(px + ((size_t)b * G * G + (size_t)(y + ky * d) * G + (x + kx * d)) * cp);
+      for (int v = 0; v < nv; v++) d0[v] = __ldg(s + v);
+    } else {
+      for (int v = 0; v < nv; v++) d0[v] = make_uint4(0, 0, 0, 0);
     }
-    col_code[j] = code;
-  }
-  __syncthreads();
-  // thread t fills row t % IM2COL_ROWS (decoded once) at columns t / IM2COL_ROWS, + 8, ...: a warp walks 32
-  // consecutive rows of one column
-  const int i = threadIdx.x % IM2COL_ROWS;
-  const int r = r0 + i;
-  int b = 0, y = -1, x = 0;
-  if (r < rows) {
-    b = r / 400;
-    const int rr = r - b * 400;
-    y = rr / 20 - 1;
-    x = rr - (rr / 20) * 20;
-  }
-  const bool on = r < rows && y >= 0 && x < 19;
-  const float* src = in + (size_t)b * cin * 361;
-  for (int j = threadIdx.x / IM2COL_ROWS; j < kpad; j += blockDim.x / IM2COL_ROWS) {
-    const int code = col_code[j];
-    float val = 0.0f;
-    if (on && code >= 0) {
-      const int yy = y + ((code >> 8) & 255) - 128, xx = x + (code & 255) - 128;
-      if (yy >= 0 && yy < 19 && xx >= 0 && xx < 19) val = __ldg(src + (size_t)(code >> 16) * 361 + yy * 19 + xx);
-    }
-    tile[i * ts + j] = from_f<T>(val);
-  }
-  __syncthreads();
-  const int per_row = kpad >> 3;
-  for (int e = threadIdx.x; e < IM2COL_ROWS * per_row; e += blockDim.x) {
-    const int i = e / per_row, g = e - i * per_row;
-    const int r = r0 + i;
-    if (r < rows)
-      *reinterpret_cast<uint4*>(out + (size_t)r * kpad + g * 8) = *reinterpret_cast<const uint4*>(tile + i * ts + g * 8);
-  }
-  if (threadIdx.x < IM2COL_ROWS) {
-    const int r = r0 + threadIdx.x;
-    if (r < rows) {
-      const int b = r / 400, rr = r - b * 400;
-      const int y = rr / 20 - 1, x = rr - (rr / 20) * 20;
-      if (y >= 0 && x < 19) rowmask[r] = __ldg(in + (size_t)b * cin * 361 + y * 19 + x);
-    }
+  } else {
+    for (int v = taps * nv; v < (kpad >> 3); v++) dst[v] = make_uint4(0, 0, 0, 0);
   }
 }
 
@@ -189,7 +178,7 @@ static __global__ void board_kernel(const __grid_constant__ BoardParams p) {
 // shared memory ([RL][CG * 8] floats, twice). C is at most 8 * POOL_THREADS; c0 and the row pitch are multiples of 8
 // (the channels up to the next multiple of 8 are read and dropped).
 // ---------------------------------------------------------------------------------------------------------------
-constexpr int POOL_THREADS = 256;
+constexpr int POOL_THREADS = 512;
 template <typename T>
 __global__ void __launch_bounds__(POOL_THREADS) pool_kernel(const T* __restrict__ x, int ld, int c0, int C,
                                                             const float* __restrict__ rowmask,
@@ -212,6 +201,7 @@ __global__ void __launch_bounds__(POOL_THREADS) pool_kernel(const T* __restrict_
       s[i] = 0.0f;
       mx[i] = -INFINITY;
     }
+#pragma unroll 4
     for (int pos = rl; pos < 361; pos += RL) {
       const int y = pos / 19, xx = pos - y * 19;
       const int r = pbl_row(b, y, xx);
@@ -306,6 +296,8 @@ __global__ void __launch_bounds__(FC_THREADS) fc_kernel(const float* __restrict_
 // the gpool-biased regular branch (bin2onnx.py :1256-1258), the policy head's p1 (:1503-1504), and the standalone
 // bn_act_mask (:1170) where a producer could not fuse it. Rows [0, rows); y's channels [C, Cw) are written as 0.
 // ---------------------------------------------------------------------------------------------------------------
+// One thread per 8 channels of a row (16-byte loads and stores); the activation fixed at compile time. x's and y's
+// row pitches and xc0 are multiples of 8 elements, Cw a multiple of 8.
 // One thread per 8 channels of a row (16-byte loads and stores); the activation fixed at compile time. x's and y's
 // row pitches and xc0 are multiples of 8 elements, Cw a multiple of 8.
 template <typename T, int ACT>
