@@ -298,8 +298,6 @@ __global__ void __launch_bounds__(FC_THREADS) fc_kernel(const float* __restrict_
 // ---------------------------------------------------------------------------------------------------------------
 // One thread per 8 channels of a row (16-byte loads and stores); the activation fixed at compile time. x's and y's
 // row pitches and xc0 are multiples of 8 elements, Cw a multiple of 8.
-// One thread per 8 channels of a row (16-byte loads and stores); the activation fixed at compile time. x's and y's
-// row pitches and xc0 are multiples of 8 elements, Cw a multiple of 8.
 template <typename T, int ACT>
 __global__ void bias_bnact_kernel(const T* __restrict__ x, int xld, int xc0, const float* __restrict__ board_bias,
                                   const float* __restrict__ scale, const float* __restrict__ bias,
