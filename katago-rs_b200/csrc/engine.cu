@@ -924,8 +924,10 @@ struct Builder {
     // attention
     const float scale = 1.0f / std::sqrt((float)hd);
     if constexpr (sizeof(T) == 2) {
-      if (hd == 64) {
+      const char* te = std::getenv("KATAGO_CUDA_TC_ATTN");
+      if (hd == 64 && vhd == 64 && !(te && te[0] == '0')) {
         // tensor-core attention (attention.cuh): Q, K and V tiles straight from the QKV rows by TMA
+        // (KATAGO_CUDA_TC_ATTN=0: the CUDA-core attention kernel below)
         if (pass == 1) {
           const int qkv_rows = rows_for(QKV);
           CUtensorMap tq = make_map(QKV.p, bf16, QKV.ld, qkv_rows, 128);
@@ -943,7 +945,7 @@ struct Builder {
           ap.err = I.d_err;
           allow_smem(attention_tc_kernel<T>, AttnCfg::SMEM);
           add(CLS_ATTN, [=](cudaStream_t st, int n) {
-            launch_pdl(attention_tc_kernel<T>, dim3(dim3(4, nh, n)), dim3(AttnCfg::THREADS), AttnCfg::SMEM, st, tq, tk, tv, ap);
+            launch_pdl(attention_tc_kernel<T>, dim3(nh, n), dim3(AttnCfg::THREADS), AttnCfg::SMEM, st, tq, tk, tv, ap);
           });
         }
         Spec so;
