@@ -64,18 +64,21 @@ CUtensorMap make_map(const void* base, bool bf16, int cols, int rows, int box_ro
 
 // A 32-row x 32-column box map with the 64-byte swizzle: the epilogue boxes (outputs and residuals) of the
 // CTA-pair GEMM.
-CUtensorMap make_box_map(const void* base, bool bf16, int cols, int rows) {
+CUtensorMap make_box_map(const void* base, bool bf16, int cols, int rows, bool f32 = false) {
   CUtensorMap map;
   cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
-  cuuint64_t strides[1] = {(cuuint64_t)cols * 2};
+  cuuint64_t strides[1] = {(cuuint64_t)cols * (f32 ? 4 : 2)};
   cuuint32_t box[2] = {32, 32};
   cuuint32_t estr[2] = {1, 1};
   if ((reinterpret_cast<uintptr_t>(base) & 15) != 0 || cols % 32 != 0)
     fail(KC_ERR_INVALID, "CUDA backend: epilogue box operand not aligned");
-  CUresult r = encode_fn()(&map, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2,
-                           const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                           CU_TENSOR_MAP_SWIZZLE_64B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                           CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  const CUtensorMapDataType dt = f32    ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32
+                                 : bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
+                                        : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  // 32 columns: 64-byte rows of a 2-byte type, 128-byte rows of float32
+  CUresult r = encode_fn()(&map, dt, 2, const_cast<void*>(base), dims, strides, box, estr,
+                           CU_TENSOR_MAP_INTERLEAVE_NONE, f32 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B,
+                           CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) fail(KC_ERR_CUDA, "CUDA backend: cuTensorMapEncodeTiled failed (" + std::to_string((int)r) + ")");
   return map;
 }
@@ -172,9 +175,10 @@ struct PairMaps {
   CUtensorMap a, b, res, raw, act;
 };
 
-template <typename T, int BN, bool WIN>
+template <typename T, int BN, bool WIN, int MODE, bool RF32>
 int launch_pair_bn(bool prepare, int pairs, cudaStream_t s, const PairMaps& m, const GemmParams& p) {
-  using C = PairCfg<BN, WIN>;
+  using C = PairCfg<BN, WIN, RF32>;
+  auto kernel = gemm_pair_kernel<T, BN, WIN, MODE, RF32>;
   cudaLaunchConfig_t cfg = {};
   cudaLaunchAttribute at[1];
   at[0].id = cudaLaunchAttributeClusterDimension;
@@ -187,10 +191,10 @@ int launch_pair_bn(bool prepare, int pairs, cudaStream_t s, const PairMaps& m, c
   cfg.attrs = at;
   cfg.numAttrs = 1;
   if (prepare) {
-    allow_smem(gemm_pair_kernel<T, BN, WIN>, C::SMEM);
+    allow_smem(kernel, C::SMEM);
     cfg.gridDim = dim3(2);
     int clusters = 0;
-    KC_CUDA(cudaOccupancyMaxActiveClusters(&clusters, gemm_pair_kernel<T, BN, WIN>, &cfg));
+    KC_CUDA(cudaOccupancyMaxActiveClusters(&clusters, kernel, &cfg));
     if (clusters <= 0) fail(KC_ERR_CUDA, "CUDA backend: no CTA pair of the trunk GEMM fits on this device");
     return clusters;
   }
@@ -200,25 +204,33 @@ int launch_pair_bn(bool prepare, int pairs, cudaStream_t s, const PairMaps& m, c
   cfg.attrs = at2;
   cfg.numAttrs = pdl_enabled() ? 2 : 1;
   cfg.gridDim = dim3(2 * pairs);
-  KC_CUDA(cudaLaunchKernelEx(&cfg, gemm_pair_kernel<T, BN, WIN>, m.a, m.b, m.res, m.raw, m.act, p));
+  KC_CUDA(cudaLaunchKernelEx(&cfg, kernel, m.a, m.b, m.res, m.raw, m.act, p));
   return pairs;
 }
 
-template <typename T, bool WIN>
-int launch_pair_w(bool prepare, int bn, int pairs, cudaStream_t s, const PairMaps& m, const GemmParams& p) {
-  switch (bn) {
-    case 128: return launch_pair_bn<T, 128, WIN>(prepare, pairs, s, m, p);
-    case 192: return launch_pair_bn<T, 192, WIN>(prepare, pairs, s, m, p);
-    case 256: return launch_pair_bn<T, 256, WIN>(prepare, pairs, s, m, p);
-    default: fail(KC_ERR_INVALID, "CUDA backend: unsupported pair tile width " + std::to_string(bn));
+// The pair kernel instances: tile width x (windowed 3x3 | linear | float32 residual | RoPE | SwiGLU), as chosen by
+// Impl::pair_tile.
+enum PairKind { PAIR_SEG = 0, PAIR_WIN = 1, PAIR_F32 = 2, PAIR_ROPE = 3, PAIR_SWIGLU = 4 };
+
+template <typename T>
+int launch_pair(bool prepare, int bn, int kind, int pairs, cudaStream_t s, const PairMaps& m, const GemmParams& p) {
+  const int key = kind * 1000 + bn;
+  switch (key) {
+    case PAIR_SEG * 1000 + 128: return launch_pair_bn<T, 128, false, MODE_SEGMENTS, false>(prepare, pairs, s, m, p);
+    case PAIR_SEG * 1000 + 192: return launch_pair_bn<T, 192, false, MODE_SEGMENTS, false>(prepare, pairs, s, m, p);
+    case PAIR_SEG * 1000 + 256: return launch_pair_bn<T, 256, false, MODE_SEGMENTS, false>(prepare, pairs, s, m, p);
+    case PAIR_WIN * 1000 + 128: return launch_pair_bn<T, 128, true, MODE_SEGMENTS, false>(prepare, pairs, s, m, p);
+    case PAIR_WIN * 1000 + 192: return launch_pair_bn<T, 192, true, MODE_SEGMENTS, false>(prepare, pairs, s, m, p);
+    case PAIR_WIN * 1000 + 256: return launch_pair_bn<T, 256, true, MODE_SEGMENTS, false>(prepare, pairs, s, m, p);
+    case PAIR_F32 * 1000 + 128: return launch_pair_bn<T, 128, false, MODE_SEGMENTS, true>(prepare, pairs, s, m, p);
+    case PAIR_F32 * 1000 + 192: return launch_pair_bn<T, 192, false, MODE_SEGMENTS, true>(prepare, pairs, s, m, p);
+    case PAIR_ROPE * 1000 + 128: return launch_pair_bn<T, 128, false, MODE_ROPE, false>(prepare, pairs, s, m, p);
+    case PAIR_SWIGLU * 1000 + 128: return launch_pair_bn<T, 128, false, MODE_SWIGLU, false>(prepare, pairs, s, m, p);
+    case PAIR_SWIGLU * 1000 + 256: return launch_pair_bn<T, 256, false, MODE_SWIGLU, false>(prepare, pairs, s, m, p);
+    default:
+      fail(KC_ERR_INVALID, "CUDA backend: unsupported pair tile (" + std::to_string(kind) + ", " + std::to_string(bn) + ")");
   }
   return 0;
-}
-
-// win: multi-tap convolution with one A window per 64-channel chunk (PairCfg)
-template <typename T>
-int launch_pair(bool prepare, int bn, bool win, int pairs, cudaStream_t s, const PairMaps& m, const GemmParams& p) {
-  return win ? launch_pair_w<T, true>(prepare, bn, pairs, s, m, p) : launch_pair_w<T, false>(prepare, bn, pairs, s, m, p);
 }
 
 // How a windowed A start that is not a multiple of 8 rows is described to tcgen05. Measured on B200: the 128 B
@@ -459,33 +471,63 @@ struct Builder {
     int rope_table_stride = 0, rope_q_cols = 0, rope_rot_cols = 0, head_dim = 0, rope_group = 1;
   };
 
-  // Tile width of the CTA-pair kernel for this GEMM, or 0 when the one-CTA kernel must run it: one or two column
-  // segments of 2-byte raw / batch-norm-activation outputs (a 2-byte residual or a per-board bias only with one
-  // segment), each kind of output in at most one segment, on 32-column-aligned operands. KATAGO_CUDA_PAIR=0 sends every GEMM to the
-  // one-CTA kernel.
-  int pair_tile(const Spec& s, const GemmParams& p) const {
+  // Tile width of the CTA-pair kernel for this GEMM, or 0 when the one-CTA kernel must run it; `f32` is set for
+  // float32 raw outputs (and residuals). Taken: one or two column segments of 2-byte raw / batch-norm-activation
+  // outputs (a 2-byte residual, a per-board bias or a masked accumulator only with one segment), each kind of output
+  // in at most one segment, on 32-column-aligned operands; one segment of float32 raw output (+ float32 residual)
+  // without an activation output; RoPE Q|K|V linears of head dim 64; SwiGLU linears. KATAGO_CUDA_PAIR=0 sends every
+  // GEMM to the one-CTA kernel.
+  int pair_tile(const Spec& s, const GemmParams& p, bool& f32) const {
+    f32 = false;
     const char* e = std::getenv("KATAGO_CUDA_PAIR");
     if (e && e[0] == '0') return 0;
-    if (s.stem || s.mode != MODE_SEGMENTS || p.nseg < 1 || p.nseg > 2) return 0;
+    if (s.stem || p.nseg < 1 || p.nseg > 2) return 0;
+    auto aligned = [](const Tensor& t, int c0) { return !t.p || (t.ld % 32 == 0 && c0 % 32 == 0); };
+    if (s.mode == MODE_ROPE || s.mode == MODE_SWIGLU) {
+      const Seg& g = s.segs[0];
+      if (p.nseg != 1 || g.raw.f32 || !aligned(g.raw, g.raw_c0)) return 0;
+      if (s.mode == MODE_ROPE) {
+        // 128 columns: two heads, one per epilogue warp of a lane quarter
+        return s.head_dim == 64 && s.N % 128 == 0 ? 128 : 0;
+      } else {
+        for (int bn : {256, 128})
+          if (s.N % bn == 0) return bn;
+      }
+      return 0;
+    }
+    if (s.mode != MODE_SEGMENTS) return 0;
     int n_raw = 0, n_act = 0, n_res = 0;
     for (int i = 0; i < p.nseg; i++) {
       const int f = p.seg[i].flags;
-      if ((f & ~(EPI_RAW | EPI_ACT | EPI_RESIDUAL | EPI_BOARD_BIAS)) || !(f & (EPI_RAW | EPI_ACT))) return 0;
+      if ((f & ~(EPI_RAW | EPI_ACT | EPI_RESIDUAL | EPI_BOARD_BIAS | EPI_MASK_ACC | EPI_RES_F32 | EPI_RAW_F32)) ||
+          !(f & (EPI_RAW | EPI_ACT)))
+        return 0;
       // per-board bias: one segment, 16-byte aligned rows (the stem)
       if ((f & EPI_BOARD_BIAS) && (p.nseg != 1 || p.seg[i].ld_bb % 4 != 0)) return 0;
+      if ((f & EPI_MASK_ACC) && p.nseg != 1) return 0;
+      const Seg& g = s.segs[i];
+      if (f & (EPI_RES_F32 | EPI_RAW_F32)) {
+        // float32 tile: one segment, raw float32 output, float32 residual if any, no activation output
+        const bool res_ok = !(f & EPI_RESIDUAL) || ((f & EPI_RES_F32) && g.res.f32);
+        if (p.nseg != 1 || !(f & EPI_RAW_F32) || !g.raw.f32 || (f & EPI_ACT) || !res_ok) return 0;
+        f32 = true;
+      } else {
+        for (const Tensor* t : {&g.res, &g.raw, &g.actout})
+          if (t->p && t->f32) return 0;
+      }
       n_raw += (f & EPI_RAW) != 0;
       n_act += (f & EPI_ACT) != 0;
       n_res += (f & EPI_RESIDUAL) != 0;
-      const Seg& g = s.segs[i];
-      for (const Tensor* t : {&g.res, &g.raw, &g.actout})
-        if (t->p && (t->f32 || t->ld % 32 != 0)) return 0;
-      if (g.res_c0 % 32 || g.raw_c0 % 32 || g.act_c0 % 32) return 0;
+      if (!aligned(g.res, g.res_c0) || !aligned(g.raw, g.raw_c0) || !aligned(g.actout, g.act_c0)) return 0;
     }
     if (n_raw > 1 || n_act > 1 || n_res > 1) return 0;
     if (p.nseg == 2 && (n_res || p.seg[0].n1 % 32)) return 0;
     if (n_act && s.N > PairCfg<256>::PARAM_COLS) return 0;
+    // float32 tiles: 256 columns would leave one pipeline stage; a masked accumulator needs a tile of 8 epilogue
+    // warps (not the 2-byte 192-wide tile)
+    const bool mask_acc = (p.seg[0].flags & EPI_MASK_ACC) != 0;
     for (int bn : {256, 192, 128})
-      if (s.N % bn == 0) return bn;
+      if (s.N % bn == 0 && !(f32 && bn == 256) && !(mask_acc && !f32 && bn == 192)) return bn;
     return 0;
   }
 
@@ -561,19 +603,6 @@ struct Builder {
       // heads (BN % (2 * head_dim))
       int bn = pick_bn(s.N, s.mode == MODE_SWIGLU ? 64 : s.mode == MODE_ROPE ? 2 * s.head_dim : 16);
       if (!bn) fail(KC_ERR_INVALID, "CUDA backend: no GEMM tile width for N = " + std::to_string(s.N));
-      std::vector<float> Wp = s.W;
-      if (s.mode == MODE_SWIGLU) {
-        // columns [0, F) = linear1, [F, 2F) = gate  ->  per tile of bn: [bn/2 linear1 | bn/2 gate]
-        const int F = s.N / 2, hb = bn / 2;
-        for (int t = 0; t < s.N / bn; t++)
-          for (int j = 0; j < hb; j++) {
-            std::memcpy(&Wp[(size_t)(t * bn + j) * K], &s.W[(size_t)(t * hb + j) * K], K * sizeof(float));
-            std::memcpy(&Wp[(size_t)(t * bn + hb + j) * K], &s.W[(size_t)(F + t * hb + j) * K], K * sizeof(float));
-          }
-      }
-      std::vector<T> Wt(Wp.size());
-      for (size_t i = 0; i < Wp.size(); i++) Wt[i] = T(Wp[i]);
-      T* dW = up(Wt);
       // KATAGO_CUDA_WIN=1: multi-tap convolutions load one A window per 64-channel chunk (the tile plus its tap
       // halo) shared by all taps. Off by default: it cuts L2 traffic by a third, but the misaligned window starts
       // cost shared-memory bandwidth the M = 128 MMA already needs (3x3 192->192 at batch 256: 94 us vs 88 us).
@@ -588,11 +617,29 @@ struct Builder {
         if (p.win_rows > TcCfg<256, true>::WIN_MAX_ROWS) win = false;
       }
       if (s.cin % 64 != 0) fail(KC_ERR_INVALID, "CUDA backend: GEMM input channels not padded");
-      if (const int pbn = win ? 0 : pair_tile(s, p)) {
-        // the trunk's GEMMs with one or two output segments: CTA-pair kernel with TMA-staged epilogue boxes; the
-        // raw, act and residual boxes each come from the (single) segment that has them
+      bool pf32 = false;
+      const int pbn = win ? 0 : pair_tile(s, p, pf32);
+      // SwiGLU tiles: the weight columns in tiles of the kernel's width
+      const int tbn = pbn ? pbn : bn;
+      std::vector<float> Wp = s.W;
+      if (s.mode == MODE_SWIGLU) {
+        // columns [0, F) = linear1, [F, 2F) = gate  ->  per tile of tbn: [tbn/2 linear1 | tbn/2 gate]
+        const int F = s.N / 2, hb = tbn / 2;
+        for (int t = 0; t < s.N / tbn; t++)
+          for (int j = 0; j < hb; j++) {
+            std::memcpy(&Wp[(size_t)(t * tbn + j) * K], &s.W[(size_t)(t * hb + j) * K], K * sizeof(float));
+            std::memcpy(&Wp[(size_t)(t * tbn + hb + j) * K], &s.W[(size_t)(F + t * hb + j) * K], K * sizeof(float));
+          }
+      }
+      std::vector<T> Wt(Wp.size());
+      for (size_t i = 0; i < Wp.size(); i++) Wt[i] = T(Wp[i]);
+      T* dW = up(Wt);
+      if (pbn) {
+        // CTA-pair kernel with TMA-staged epilogue boxes (the trunk's convolutions, the token linears); the raw,
+        // act and residual boxes each come from the (single) segment that has them
         const Tensor *raw = nullptr, *act = nullptr, *res = nullptr;
         p.pair_split = p.nseg > 1 ? p.seg[0].n1 : p.n_total;
+        if (s.mode != MODE_SEGMENTS) raw = &s.segs[0].raw, p.pair_raw_x = s.segs[0].raw_c0;  // RoPE / SwiGLU
         for (int i = 0; i < p.nseg; i++) {
           const Seg& g = s.segs[i];
           const int n0 = p.seg[i].n0;
@@ -602,10 +649,10 @@ struct Builder {
         }
         const Tensor& out0 = raw ? *raw : *act;
         auto box = [&](const Tensor* t) { return make_box_map(t ? t->p : out0.p, bf16, t ? t->ld : out0.ld,
-                                                              rows_for(t ? *t : out0)); };
+                                                              rows_for(t ? *t : out0), t && t->f32); };
         // 3x3 convolutions read one A window per 64-channel chunk (KATAGO_CUDA_PAIR_WIN=0: one A tile per tap)
         const char* pw = std::getenv("KATAGO_CUDA_PAIR_WIN");
-        bool pwin = p.taps == PairCfg<256, true>::WIN_TAPS && !(pw && pw[0] == '0');
+        bool pwin = p.taps == PairCfg<256, true>::WIN_TAPS && !pf32 && !(pw && pw[0] == '0');
         if (pwin) {
           int halo = 0;
           for (int i = 0; i < p.taps; i++) halo = std::max(halo, std::abs(p.tap_off[i]));
@@ -619,18 +666,19 @@ struct Builder {
         pm.res = box(res);
         pm.raw = box(raw);
         pm.act = box(act);
-        const int max_pairs = launch_pair<T>(true, pbn, pwin, 0, 0, pm, p);
+        const int kind = s.mode == MODE_ROPE ? PAIR_ROPE : s.mode == MODE_SWIGLU ? PAIR_SWIGLU : pf32 ? PAIR_F32
+                         : pwin ? PAIR_WIN : PAIR_SEG;
+        const int max_pairs = launch_pair<T>(true, pbn, kind, 0, 0, pm, p);
         add(s.cls, [=](cudaStream_t st, int n) {
           GemmParams q = p;
           q.g.rows = n * brows;
           const int tiles = ((q.g.rows + 255) / 256) * (q.n_total / pbn);
-          launch_pair<T>(false, pbn, pwin, std::min(tiles, max_pairs), st, pm, q);
+          launch_pair<T>(false, pbn, kind, std::min(tiles, max_pairs), st, pm, q);
         });
         return;
       }
       CUtensorMap ta = make_map(s.A.p, bf16, s.A.ld, a_rows, win ? p.win_rows : 128);
       CUtensorMap tb = make_map(dW, bf16, K, s.N, bn);
-      if (s.cin % 64 != 0) fail(KC_ERR_INVALID, "CUDA backend: GEMM input channels not padded");
       bool rf32 = false;
       for (int i = 0; i < p.nseg; i++) rf32 = rf32 || (p.seg[i].flags & EPI_RES_F32);
       launch_tc<T>(true, rf32, win, bn, 0, 0, ta, tb, p);
@@ -776,10 +824,27 @@ struct Builder {
                                                                     out_stride, n);
     });
   }
+  // The row RMSNorm kernel with 128-bit loads takes C = 128 k channels (k <= 8) on 4-element-aligned rows.
+  static bool rms_vec(Tensor x, int C, Tensor y) {
+    return C % 128 == 0 && C <= 1024 && x.ld % 4 == 0 && y.ld % 4 == 0;
+  }
+
   void rmsnorm(Tensor x, int C, const TfRmsDesc& d, Tensor y) {
     const float* w = up(d.w);
     float eps = d.eps;
     Engine::Impl* Ip = &I;
+    if (rms_vec(x, C, y)) {
+      add(CLS_OTHER, [=](cudaStream_t st, int n) {
+        const int rows = n * 400;
+        if (x.f32)
+          launch_pdl(rms_rows_kernel<float, T, false>, dim3((rows + 7) / 8), dim3(256), 0, st, (const float*)x.p,
+                     x.ld, C / 128, w, (const float*)nullptr, 0, eps, Ip->rowmask, rows, (T*)y.p, y.ld);
+        else
+          launch_pdl(rms_rows_kernel<T, T, false>, dim3((rows + 7) / 8), dim3(256), 0, st, (const T*)x.p, x.ld,
+                     C / 128, w, (const float*)nullptr, 0, eps, Ip->rowmask, rows, (T*)y.p, y.ld);
+      });
+      return;
+    }
     add(CLS_OTHER, [=](cudaStream_t st, int n) {
       int rows = n * 400;
       if (x.f32)
@@ -1166,14 +1231,27 @@ struct Builder {
       int spatial = m.tip_rms_spatial ? 1 : 0;
       int act = m.tip_act;
       Engine::Impl* Ip = &I;
-      add(CLS_OTHER, [=](cudaStream_t st, int n) {
-        if (X.f32)
-          launch_pdl(tip_rms_kernel<float, T>, dim3(n), dim3(512), 0, st, (const float*)X.p, X.ld, C, g, bb, eps, spatial, act,
-                                                      Ip->rowmask, Ip->mask_sum, (T*)XA.p, XA.ld);
-        else
-          launch_pdl(tip_rms_kernel<T, T>, dim3(n), dim3(512), 0, st, (const T*)X.p, X.ld, C, g, bb, eps, spatial, act, Ip->rowmask,
-                                                  Ip->mask_sum, (T*)XA.p, XA.ld);
-      });
+      if (!spatial && rms_vec(X, C, XA)) {
+        // per-point tip: one warp per row
+        add(CLS_OTHER, [=](cudaStream_t st, int n) {
+          const int rows = n * 400;
+          if (X.f32)
+            launch_pdl(rms_rows_kernel<float, T, true>, dim3((rows + 7) / 8), dim3(256), 0, st, (const float*)X.p,
+                       X.ld, C / 128, g, bb, act, eps, Ip->rowmask, rows, (T*)XA.p, XA.ld);
+          else
+            launch_pdl(rms_rows_kernel<T, T, true>, dim3((rows + 7) / 8), dim3(256), 0, st, (const T*)X.p, X.ld,
+                       C / 128, g, bb, act, eps, Ip->rowmask, rows, (T*)XA.p, XA.ld);
+        });
+      } else {
+        add(CLS_OTHER, [=](cudaStream_t st, int n) {
+          if (X.f32)
+            launch_pdl(tip_rms_kernel<float, T>, dim3(n), dim3(512), 0, st, (const float*)X.p, X.ld, C, g, bb, eps, spatial, act,
+                                                        Ip->rowmask, Ip->mask_sum, (T*)XA.p, XA.ld);
+          else
+            launch_pdl(tip_rms_kernel<T, T>, dim3(n), dim3(512), 0, st, (const T*)X.p, X.ld, C, g, bb, eps, spatial, act, Ip->rowmask,
+                                                    Ip->mask_sum, (T*)XA.p, XA.ld);
+        });
+      }
     }
     // heads: one GEMM for p1 | g1 | v1 (bin2onnx.py policy_head :1495, value_head :1518)
     const int p1c = m.p1_conv.oc, g1c = m.g1_conv.oc, v1c = m.v1_conv.oc;

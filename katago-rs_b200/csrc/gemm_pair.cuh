@@ -2,9 +2,16 @@
 // CTA), operand tiles by TMA in 128-channel pipeline stages, accumulators in TMEM, and an epilogue that stages each
 // 32 x 32 output box in shared memory and writes it with a TMA store (residuals arrive the same way, by TMA loads).
 //
-// It computes what gemm_tc_kernel computes for one-segment GEMMs with 2-byte outputs and residuals
-// (the raw / residual / batch-norm-activation epilogue of bin2onnx.py residual_block :1243-1248 and
-// nested_bottleneck_block :1263-1269): y = A * W^T (+ residual); raw = y * mask; act = act(y * scale + bias) * mask.
+// It computes what gemm_tc_kernel computes for
+//  * MODE_SEGMENTS: one or two column segments of 2-byte outputs and residuals (the raw / residual /
+//    batch-norm-activation epilogue of bin2onnx.py residual_block :1243-1248 and nested_bottleneck_block
+//    :1263-1269): y = A * W^T (* mask) (+ residual); raw = y * mask; act = act(y * scale + bias) * mask. RF32: the
+//    residual and the raw output are float32 (the bf16 tier's residual stream; transformer_attention_block and
+//    transformer_ffn_block's output linears, :1359-1438, with the branch output masked before the add);
+//  * MODE_ROPE: the attention block's Q|K|V linear with 2D RoPE on the Q and K heads (head dim 64, the head's two
+//    rotation halves at columns [0, 32) and [32, 64), :1369-1374 and :449-484): one head per epilogue warp;
+//  * MODE_SWIGLU: the FFN's first linear and gate, SiLU(x W1) * (x Wg) * mask (:1425-1438), each tile's columns
+//    [linear1 | gate] halves.
 //
 // Why the layout is what it is (measured on B200):
 //  * tcgen05.mma issue blocks the issuing thread once about four MMAs are queued, and each barrier wait + commit
@@ -24,9 +31,10 @@ namespace kc {
 // window travels with its chunk's first stage, on that stage's barrier: no barriers of its own. Slot ch % 2 is free
 // when that stage's slot is (its MMAs follow chunk ch - 2's whenever STAGES <= 4, with 3 stages per chunk). This cuts the TMA bytes of a
 // 3x3 convolution's K-block from 28 KB to about 14 KB per CTA, below what TMA delivers per SM.
-template <int BN, bool WIN = false>
+template <int BN, bool WIN = false, bool RF32 = false>
 struct PairCfg {
   static_assert(BN % 64 == 0 && BN >= 64 && BN <= 256, "pair tile width");
+  static_assert(!(WIN && RF32), "float32 residual tiles are linears");
   static constexpr int BH = BN / 2;               // B rows (output columns) staged by each CTA of the pair
   static constexpr int A_BYTES = 128 * 64 * 2;    // one 64-channel K-block of this CTA's 128 rows
   static constexpr int B_BYTES = BH * 64 * 2;     // one K-block of this CTA's half of the weights
@@ -38,18 +46,23 @@ struct PairCfg {
   static constexpr int A_WIN_BYTES = WIN_MAX_ROWS * 128;
   static constexpr int A_RING_BYTES = WIN ? 2 * A_WIN_BYTES : 0;
   // Epilogue warps: 2 or (1x1 tiles of BN = 192, whose time is the epilogue's) 3 per TMEM lane quarter, splitting
-  // the tile's columns; the windowed 3x3 keeps 2 (its third weight stage is worth more). With 12 epilogue warps
+  // the tile's columns; the windowed 3x3 keeps 2 (its third weight stage is worth more), and so do float32
+  // residual tiles (their boxes are twice as large). With 12 epilogue warps
   // the CTA has 16 (512 threads, 128 registers each at launch) and setmaxnreg moves registers from warpgroup 0
   // (TMA producer, MMA issuer, two idle warps: 56 each) to the three epilogue warpgroups (152 each):
   // 4 x 32 x 56 + 12 x 32 x 152 = 65,536, and per SMSP 56 + 3 x 152 = 512 x 32 = 16,384.
-  static constexpr int EPI_WARPS = BN == 192 && !WIN ? 12 : 8;
+  static constexpr int EPI_WARPS = BN == 192 && !WIN && !RF32 ? 12 : 8;
   static constexpr int EPI_WARP0 = EPI_WARPS == 12 ? 4 : 2;  // first epilogue warp (a warpgroup boundary with 12)
   static constexpr int WG0_REGS = 56, EPI_REGS = 152;
   static constexpr int WARP_COLS = BN / (EPI_WARPS / 4);
   static constexpr int CHUNKS = WARP_COLS / 32;   // 32-column boxes per warp and tile
-  static constexpr int BOX_BYTES = 32 * 32 * 2;   // 32 rows x 32 columns of a 2-byte type (64-byte swizzle)
-  static constexpr int NRES = WIN || BN > 128 ? 2 : 4;  // residual boxes in flight per epilogue warp (as fits)
-  static constexpr int EPI_WARP_BYTES = (2 + NRES) * BOX_BYTES;  // raw box, act box, residual ring
+  // staging boxes of 32 rows x 32 columns: 2-byte outputs in 64-byte rows (64-byte swizzle), float32 raw outputs
+  // and residuals in 128-byte rows (128-byte swizzle)
+  static constexpr int BOX_BYTES = 32 * 32 * 2;
+  static constexpr int RBOX_BYTES = RF32 ? 32 * 32 * 4 : BOX_BYTES;  // raw output and residual boxes
+  static constexpr int ABOX_BYTES = RF32 ? 0 : BOX_BYTES;            // act output box (none with RF32)
+  static constexpr int NRES = WIN || RF32 || BN > 128 ? 2 : 4;  // residual boxes in flight per epilogue warp
+  static constexpr int EPI_WARP_BYTES = RBOX_BYTES + ABOX_BYTES + NRES * RBOX_BYTES;  // raw, act, residual ring
   static constexpr int EPI_BYTES = EPI_WARPS * EPI_WARP_BYTES;
   static constexpr int PARAM_COLS = 768;          // per-column BN scale / bias in shared memory
   static constexpr int PARAM_BYTES = 2 * PARAM_COLS * 4;
@@ -98,6 +111,15 @@ __device__ __forceinline__ void stage_row(uint8_t* box, int r, const float (&o)[
     u.w = pack2<T>(o[8 * j + 6], o[8 * j + 7]);
     *reinterpret_cast<uint4*>(box + sw64_off(r, j)) = u;
   }
+}
+
+// Write 32 floats of this thread's row into a 128-byte-swizzled float32 staging box (CU_TENSOR_MAP_SWIZZLE_128B:
+// 16-byte chunk j of row r at chunk j ^ (r % 8); conflict-free for the 8 threads of a 128-bit store phase).
+__device__ __forceinline__ void stage_row_f32(uint8_t* box, int r, const float (&o)[32]) {
+#pragma unroll
+  for (int j = 0; j < 8; j++)
+    *reinterpret_cast<float4*>(box + r * 128 + ((j ^ (r & 7)) << 4)) =
+        make_float4(o[4 * j], o[4 * j + 1], o[4 * j + 2], o[4 * j + 3]);
 }
 
 // Packed two-lane float32 arithmetic (sm_100 fma / mul / add .f32x2): two elements per instruction, float32
@@ -177,12 +199,15 @@ __device__ __forceinline__ void pair_act(const float (&v)[32], const float* sc, 
   }
 }
 
-template <typename T, int BN, bool WIN>
-__global__ void __launch_bounds__(PairCfg<BN, WIN>::THREADS, 1)
+template <typename T, int BN, bool WIN, int MODE = MODE_SEGMENTS, bool RF32 = false>
+__global__ void __launch_bounds__(PairCfg<BN, WIN, RF32>::THREADS, 1)
     gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                      const __grid_constant__ CUtensorMap tmRes, const __grid_constant__ CUtensorMap tmRaw,
                      const __grid_constant__ CUtensorMap tmAct, const __grid_constant__ GemmParams p) {
-  using C = PairCfg<BN, WIN>;
+  using C = PairCfg<BN, WIN, RF32>;
+  static_assert(MODE != MODE_ROPE || C::WARP_COLS == 64, "RoPE tiles give each epilogue warp one head of 64");
+  static_assert(MODE != MODE_SWIGLU || (BN % 128 == 0 && C::EPI_WARPS == 8), "SwiGLU tile halves");
+  static_assert(MODE == MODE_SEGMENTS || (!WIN && !RF32), "RoPE / SwiGLU tiles are linears");
   constexpr int fmt = std::is_same<T, __nv_bfloat16>::value ? 1 : 0;
   constexpr uint32_t IDESC = make_idesc_f16(fmt, 256, BN);
 
@@ -431,7 +456,8 @@ __global__ void __launch_bounds__(PairCfg<BN, WIN>::THREADS, 1)
     const int h = ew >> 2;
     uint8_t* wbuf = epi + ew * C::EPI_WARP_BYTES;
     uint8_t* st_raw = wbuf;
-    uint8_t* st_act = wbuf + C::BOX_BYTES;
+    uint8_t* st_act = wbuf + C::RBOX_BYTES;  // RoPE: the head's second rotation half
+    constexpr int RES_OFF = C::RBOX_BYTES + C::ABOX_BYTES;  // the residual ring after the raw and act boxes
     uint64_t* rb = rbar + C::NRES * ew;
     const bool has_res = (flags & EPI_RESIDUAL) != 0;  // one-segment GEMMs only
     const int a0 = p.seg[0].act, a1 = p.nseg > 1 ? p.seg[1].act : a0;
@@ -446,8 +472,8 @@ __global__ void __launch_bounds__(PairCfg<BN, WIN>::THREADS, 1)
       if (tile >= num_tiles) return;
       const int mrow = (tile / n_tiles) * 256 + (int)rank * 128 + q * 32;
       const int col = (tile % n_tiles) * BN + h * C::WARP_COLS + c * 32;
-      mbar_expect_tx(&rb[u % C::NRES], C::BOX_BYTES);
-      tma_load_2d(wbuf + (2 + u % C::NRES) * C::BOX_BYTES, &tmRes, &rb[u % C::NRES], res_x + col, mrow);
+      mbar_expect_tx(&rb[u % C::NRES], C::RBOX_BYTES);
+      tma_load_2d(wbuf + RES_OFF + (u % C::NRES) * C::RBOX_BYTES, &tmRes, &rb[u % C::NRES], res_x + col, mrow);
     };
     if (has_res && lane == 0)
       for (int i = 0; i < C::NRES; i++) res_issue(i);
@@ -468,80 +494,174 @@ __global__ void __launch_bounds__(PairCfg<BN, WIN>::THREADS, 1)
       }
       __syncwarp();
       tc_fence_after();
-      const uint32_t tacc = tmem_base + acc * C::ACC_COLS + ((uint32_t)(q * 32) << 16) + h * C::WARP_COLS;
+      if constexpr (MODE == MODE_SEGMENTS) {
+        const uint32_t tacc = tmem_base + acc * C::ACC_COLS + ((uint32_t)(q * 32) << 16) + h * C::WARP_COLS;
 #pragma unroll 1
-      for (int c = 0; c < C::CHUNKS; c++, u++) {
-        uint32_t x[32];
-        tmem_ld32(tacc + c * 32, x);
-        tmem_wait_ld();
-        if (c == C::CHUNKS - 1) {
-          // the accumulator is in registers: hand it back to the MMA issuer before the math
-          tc_fence_before();
+        for (int c = 0; c < C::CHUNKS; c++, u++) {
+          uint32_t x[32];
+          tmem_ld32(tacc + c * 32, x);
+          tmem_wait_ld();
+          if (c == C::CHUNKS - 1) {
+            // the accumulator is in registers: hand it back to the MMA issuer before the math
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive_cluster(tempty_leader0 + acc * 8);
+          }
+          float v[32];
+#pragma unroll
+          for (int i = 0; i < 32; i++) v[i] = __uint_as_float(x[i]);
+          if ((f0 & EPI_BOARD_BIAS) && m != 0.0f) {
+            // per-board bias (one-segment GEMMs: the stem's global-feature term), 32 columns of this row's board
+            const float* bb = p.seg[0].board_bias + (size_t)(r / 400) * p.seg[0].ld_bb + ncol0 + c * 32;
+#pragma unroll
+            for (int j = 0; j < 32; j += 4) {
+              const float4 q = __ldg(reinterpret_cast<const float4*>(bb + j));
+              v[j] += q.x;
+              v[j + 1] += q.y;
+              v[j + 2] += q.z;
+              v[j + 3] += q.w;
+            }
+          }
+          // one-segment GEMMs of 8 epilogue warps (the 12-warp tiles have no registers to spare): the transformer
+          // branch output is masked before the add
+          if (C::EPI_WARPS == 8 && (f0 & EPI_MASK_ACC)) {
+#pragma unroll
+            for (int i = 0; i < 32; i++) v[i] *= m;
+          }
+          if (has_res) {
+            if (!mbar_wait(&rb[u % C::NRES], (u / C::NRES) & 1, p.err, DEV_TIMEOUT_EPILOGUE)) {
+              *abort_flag = 1;
+              ok = false;
+              break;
+            }
+            const uint8_t* rbox = wbuf + RES_OFF + (u % C::NRES) * C::RBOX_BYTES;
+            if constexpr (RF32) {
+#pragma unroll
+              for (int j = 0; j < 8; j++) {
+                const float4 w = *reinterpret_cast<const float4*>(rbox + lane * 128 + ((j ^ (lane & 7)) << 4));
+                v[4 * j] += w.x;
+                v[4 * j + 1] += w.y;
+                v[4 * j + 2] += w.z;
+                v[4 * j + 3] += w.w;
+              }
+            } else {
+#pragma unroll
+              for (int j = 0; j < 4; j++) {
+                uint4 w = *reinterpret_cast<const uint4*>(rbox + sw64_off(lane, j));
+                const T* e = reinterpret_cast<const T*>(&w);
+#pragma unroll
+                for (int k = 0; k < 8; k++) v[8 * j + k] += to_f<T>(e[k]);
+              }
+            }
+            __syncwarp();
+            if (lane == 0) {
+              fence_proxy_async_smem();
+              res_issue(u + C::NRES);
+            }
+          }
+          // the previous box's stores must have read the staging boxes before they are overwritten
+          if (lane == 0) bulk_wait_read0();
           __syncwarp();
-          if (lane == 0) mbar_arrive_cluster(tempty_leader0 + acc * 8);
-        }
-        float v[32];
+          const int col = ncol0 + c * 32;
+          const int cf = col < split ? f0 : f1;  // this box's segment
+          if (cf & EPI_RAW) {
+            float o[32];
 #pragma unroll
-        for (int i = 0; i < 32; i++) v[i] = __uint_as_float(x[i]);
-        if ((f0 & EPI_BOARD_BIAS) && m != 0.0f) {
-          // per-board bias (one-segment GEMMs: the stem's global-feature term), 32 columns of this row's board
-          const float* bb = p.seg[0].board_bias + (size_t)(r / 400) * p.seg[0].ld_bb + ncol0 + c * 32;
-#pragma unroll
-          for (int j = 0; j < 32; j += 4) {
-            const float4 q = __ldg(reinterpret_cast<const float4*>(bb + j));
-            v[j] += q.x;
-            v[j + 1] += q.y;
-            v[j + 2] += q.z;
-            v[j + 3] += q.w;
+            for (int i = 0; i < 32; i++) o[i] = v[i] * m;
+            if constexpr (RF32) stage_row_f32(st_raw, lane, o);
+            else stage_row<T>(st_raw, lane, o);
           }
-        }
-        if (has_res) {
-          if (!mbar_wait(&rb[u % C::NRES], (u / C::NRES) & 1, p.err, DEV_TIMEOUT_EPILOGUE)) {
-            *abort_flag = 1;
-            ok = false;
-            break;
+          if (!RF32 && (cf & EPI_ACT)) {
+            float o[32];
+            switch (col < split ? a0 : a1) {
+              case 1: pair_act<1>(v, s_scale + col, s_bias + col, m, o); break;
+              case 2: pair_act<2>(v, s_scale + col, s_bias + col, m, o); break;
+              case 3: pair_act<3>(v, s_scale + col, s_bias + col, m, o); break;
+              default: pair_act<0>(v, s_scale + col, s_bias + col, m, o); break;
+            }
+            stage_row<T>(st_act, lane, o);
           }
-          const uint8_t* rbox = wbuf + (2 + u % C::NRES) * C::BOX_BYTES;
-#pragma unroll
-          for (int j = 0; j < 4; j++) {
-            uint4 w = *reinterpret_cast<const uint4*>(rbox + sw64_off(lane, j));
-            const T* e = reinterpret_cast<const T*>(&w);
-#pragma unroll
-            for (int k = 0; k < 8; k++) v[8 * j + k] += to_f<T>(e[k]);
-          }
+          fence_proxy_async_smem();
           __syncwarp();
           if (lane == 0) {
-            fence_proxy_async_smem();
-            res_issue(u + C::NRES);
+            if (cf & EPI_RAW) tma_store_2d(&tmRaw, st_raw, raw_x + col, mrow);
+            if (!RF32 && (cf & EPI_ACT)) tma_store_2d(&tmAct, st_act, act_x + col, mrow);
+            bulk_commit_group();
           }
         }
-        // the previous box's stores must have read the staging boxes before they are overwritten
+      } else if constexpr (MODE == MODE_ROPE) {
+        // one head of 64 columns per warp: Q and K heads rotated in halves of 32 (x0 at [0, 32), x1 at [32, 64)),
+        // V heads as they are; cos / sin of this row's board point from the head's table (L2-resident)
+        const int rr = r % 400, py = rr / 20 - 1, px = rr % 20;
+        const int pos = py >= 0 && py < 19 && px < 19 ? py * 19 + px : 0;
+        const bool rot = ncol0 < p.rope_rot_cols;
+        const int head = ncol0 / 64;
+        const int table = ncol0 < p.rope_q_cols ? head / p.rope_group : head - p.rope_q_cols / 64;
+        const size_t toff = (size_t)table * p.rope_table_stride + (size_t)pos * 32;
+        const uint32_t tacc = tmem_base + acc * C::ACC_COLS + ((uint32_t)(q * 32) << 16) + h * C::WARP_COLS;
+        uint32_t x0[32], x1[32];
+        tmem_ld32(tacc, x0);
+        tmem_ld32(tacc + 32, x1);
+        tmem_wait_ld();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive_cluster(tempty_leader0 + acc * 8);
+        float o0[32], o1[32];
+#pragma unroll
+        for (int j = 0; j < 32; j += 4) {
+          float4 cs = make_float4(1.0f, 1.0f, 1.0f, 1.0f), sn = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+          if (rot) {
+            cs = __ldg(reinterpret_cast<const float4*>(p.rope_cos + toff + j));
+            sn = __ldg(reinterpret_cast<const float4*>(p.rope_sin + toff + j));
+          }
+          const float c4[4] = {cs.x, cs.y, cs.z, cs.w}, s4[4] = {sn.x, sn.y, sn.z, sn.w};
+#pragma unroll
+          for (int i = 0; i < 4; i++) {
+            const float a = __uint_as_float(x0[j + i]), b = __uint_as_float(x1[j + i]);
+            o0[j + i] = (a * c4[i] - b * s4[i]) * m;
+            o1[j + i] = (a * s4[i] + b * c4[i]) * m;
+          }
+        }
         if (lane == 0) bulk_wait_read0();
         __syncwarp();
-        const int col = ncol0 + c * 32;
-        const int cf = col < split ? f0 : f1;  // this box's segment
-        if (cf & EPI_RAW) {
-          float o[32];
-#pragma unroll
-          for (int i = 0; i < 32; i++) o[i] = v[i] * m;
-          stage_row<T>(st_raw, lane, o);
-        }
-        if (cf & EPI_ACT) {
-          float o[32];
-          switch (col < split ? a0 : a1) {
-            case 1: pair_act<1>(v, s_scale + col, s_bias + col, m, o); break;
-            case 2: pair_act<2>(v, s_scale + col, s_bias + col, m, o); break;
-            case 3: pair_act<3>(v, s_scale + col, s_bias + col, m, o); break;
-            default: pair_act<0>(v, s_scale + col, s_bias + col, m, o); break;
-          }
-          stage_row<T>(st_act, lane, o);
-        }
+        stage_row<T>(st_raw, lane, o0);
+        stage_row<T>(st_act, lane, o1);
         fence_proxy_async_smem();
         __syncwarp();
         if (lane == 0) {
-          if (cf & EPI_RAW) tma_store_2d(&tmRaw, st_raw, raw_x + col, mrow);
-          if (cf & EPI_ACT) tma_store_2d(&tmAct, st_act, act_x + col, mrow);
+          tma_store_2d(&tmRaw, st_raw, raw_x + ncol0, mrow);
+          tma_store_2d(&tmRaw, st_act, raw_x + ncol0 + 32, mrow);
           bulk_commit_group();
+        }
+      } else {
+        // SwiGLU: this warp's BN / 4 output columns, linear1 at accumulator columns [h BN / 4, ...) of the tile's
+        // first half and the gate at the same place in its second half
+        constexpr int OCH = BN / 128;
+        const int ocol0 = (tile % n_tiles) * (BN / 2) + h * (BN / 4);
+        const uint32_t tacc = tmem_base + acc * C::ACC_COLS + ((uint32_t)(q * 32) << 16) + h * (BN / 4);
+#pragma unroll 1
+        for (int c = 0; c < OCH; c++) {
+          uint32_t xa[32], xg[32];
+          tmem_ld32(tacc + c * 32, xa);
+          tmem_ld32(tacc + BN / 2 + c * 32, xg);
+          tmem_wait_ld();
+          if (c == OCH - 1) {
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive_cluster(tempty_leader0 + acc * 8);
+          }
+          float o[32];
+#pragma unroll
+          for (int i = 0; i < 32; i++) o[i] = act_fn<3>(__uint_as_float(xa[i])) * __uint_as_float(xg[i]) * m;
+          if (lane == 0) bulk_wait_read0();
+          __syncwarp();
+          stage_row<T>(st_raw, lane, o);
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) {
+            tma_store_2d(&tmRaw, st_raw, raw_x + ocol0 + c * 32, mrow);
+            bulk_commit_group();
+          }
         }
       }
     }

@@ -380,6 +380,91 @@ __global__ void rmsnorm_kernel(const TI* __restrict__ x, int ld, int C, const fl
 }
 
 // ---------------------------------------------------------------------------------------------------------------
+// Row RMSNorm with 128-bit loads: one warp per PBL row, the row's C channels (C = 128 nv, nv <= 8) held in
+// registers as 4-channel vectors (lane l holds channels 128 i + 4 l .. + 3). TIP = false: the transformer block
+// norm, y = x * rms * w * mask (bin2onnx.py transformer_rmsnorm :1330-1340); TIP = true: the per-point trunk tip,
+// y = act(x * rms * gamma + beta) * mask (trunk_tip_rmsnorm :1440-1463). rms = 1 / sqrt(sum(x^2) / C + eps).
+// ---------------------------------------------------------------------------------------------------------------
+template <typename U>
+__device__ __forceinline__ float4 load4(const U* p) {
+  if constexpr (std::is_same<U, float>::value) {
+    return *reinterpret_cast<const float4*>(p);
+  } else {
+    const uint2 u = *reinterpret_cast<const uint2*>(p);
+    const U* e = reinterpret_cast<const U*>(&u);
+    return make_float4(to_f<U>(e[0]), to_f<U>(e[1]), to_f<U>(e[2]), to_f<U>(e[3]));
+  }
+}
+
+template <typename U>
+__device__ __forceinline__ void store4(U* p, float a, float b, float c, float d) {
+  if constexpr (std::is_same<U, float>::value) {
+    *reinterpret_cast<float4*>(p) = make_float4(a, b, c, d);
+    return;
+  }
+  uint2 u;
+  U* e = reinterpret_cast<U*>(&u);
+  e[0] = from_f<U>(a);
+  e[1] = from_f<U>(b);
+  e[2] = from_f<U>(c);
+  e[3] = from_f<U>(d);
+  *reinterpret_cast<uint2*>(p) = u;
+}
+
+template <typename TI, typename T, bool TIP>
+__global__ void rms_rows_kernel(const TI* __restrict__ x, int ld, int nv, const float* __restrict__ w,
+                                const float* __restrict__ beta, int act, float eps,
+                                const float* __restrict__ rowmask, int rows, T* __restrict__ y, int yld) {
+  pdl_wait();
+  pdl_trigger();
+  const int r = blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
+  const int lane = threadIdx.x & 31;
+  if (r >= rows) return;
+  const TI* xr = x + (size_t)r * ld + lane * 4;
+  float4 v[8];
+  float ss = 0.0f;
+#pragma unroll
+  for (int i = 0; i < 8; i++) {
+    if (i < nv) {
+      v[i] = load4<TI>(xr + i * 128);
+      ss += v[i].x * v[i].x;
+      ss += v[i].y * v[i].y;
+      ss += v[i].z * v[i].z;
+      ss += v[i].w * v[i].w;
+    }
+  }
+  for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+  const float ms = ss / (float)(nv * 128);
+  const float den = sqrtf(ms + eps);
+  const float rms = 1.0f / den;
+  const float m = rowmask[r];
+  T* yr = y + (size_t)r * yld + lane * 4;
+#pragma unroll
+  for (int i = 0; i < 8; i++) {
+    if (i < nv) {
+      const int c = i * 128 + lane * 4;
+      const float4 g = __ldg(reinterpret_cast<const float4*>(w + c));
+      float o[4] = {v[i].x * rms, v[i].y * rms, v[i].z * rms, v[i].w * rms};
+      const float gg[4] = {g.x, g.y, g.z, g.w};
+      if constexpr (TIP) {
+        const float4 bt = __ldg(reinterpret_cast<const float4*>(beta + c));
+        const float bb[4] = {bt.x, bt.y, bt.z, bt.w};
+#pragma unroll
+        for (int k = 0; k < 4; k++) {
+          float t = o[k] * gg[k];
+          t = t + bb[k];
+          o[k] = act_apply(t, act) * m;
+        }
+      } else {
+#pragma unroll
+        for (int k = 0; k < 4; k++) o[k] = o[k] * gg[k] * m;
+      }
+      store4<T>(yr + i * 128, o[0], o[1], o[2], o[3]);
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------------------------------------------
 // Trunk-tip RMSNorm (bin2onnx.py trunk_tip_rmsnorm :1440-1463): act(x * rms * gamma + beta) * mask, rms per point
 // over channels, or (spatial) one rms per board over channels x on-board points. One block per board.
 // ---------------------------------------------------------------------------------------------------------------

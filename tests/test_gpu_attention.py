@@ -17,6 +17,11 @@ pytestmark = pytest.mark.gpu
 
 KEYS = ("policy", "value", "scorevalue", "ownership")
 TOL = 2e-2
+# bf16 keeps 8 significant bits. On these random-init transformer nets (policy logits up to |3|) the bf16 tier's
+# outputs sit 0.013-0.022 from the float64 oracle whichever attention and GEMM kernels run (the error of bf16 storage
+# of the branch inputs, Q|K|V, P and the SwiGLU output over 20 residual branches), so bf16 cases are held to 3e-2
+# and f16 cases to the 2e-2 tier.
+TOL_BF16_NET = 3e-2
 
 
 def handle(m, prec, n, tc):
@@ -54,18 +59,20 @@ def test_gqa_mixed_boards_f16(n):
 
 
 def test_gqa_mixed_boards_bf16():
-    """bf16 storage alone puts this net's policy logits 0.020-0.021 from the float64 oracle with either attention
-    kernel, so at bf16 the tensor-core kernel is held to the CUDA-core attention kernel (KATAGO_CUDA_TC_ATTN=0)."""
+    """At bf16 the tensor-core attention kernel and the CUDA-core one (KATAGO_CUDA_TC_ATTN=0) are each held to the
+    bf16 bound below (two bf16 runs whose roundings diverge differ by about as much as either differs from the
+    oracle)."""
     n = 13
     m, x = case("gqa-tf", n, 4321 + n, (9, 13, 19))
-    got = handle(m, kc.PRECISION_BF16, n, "1").forward(*x)
-    ref = handle(m, kc.PRECISION_BF16, n, "0").forward(*x)
-    errs = max_err(got, ref)
-    assert max(errs.values()) <= TOL, errs
+    want = OracleNet(netgen.net_bytes("gqa-tf")).forward(*x)
+    for tc in ("1", "0"):
+        errs = max_err(handle(m, kc.PRECISION_BF16, n, tc).forward(*x), want)
+        assert max(errs.values()) <= TOL_BF16_NET, (tc, errs)
 
 
-def test_b10c384h6_bf16():
+@pytest.mark.parametrize("prec,tol", [(kc.PRECISION_F16, TOL), (kc.PRECISION_BF16, TOL_BF16_NET)])
+def test_b10c384h6(prec, tol):
     m, x = case("b10c384h6", 3, 77, (19, 13))
-    got = handle(m, kc.PRECISION_BF16, 3, "1").forward(*x)
+    got = handle(m, prec, 3, "1").forward(*x)
     errs = max_err(got, OracleNet(netgen.net_bytes("b10c384h6")).forward(*x))
-    assert max(errs.values()) <= TOL, errs
+    assert max(errs.values()) <= tol, errs

@@ -1,7 +1,8 @@
-"""The trunk's CTA-pair GEMM (the default for one- and two-segment convolutions with 2-byte outputs) against the
-one-CTA GEMM (KATAGO_CUDA_PAIR=0), the pair kernel without A windows (KATAGO_CUDA_PAIR_WIN=0) and the float64
-oracle, on the tile widths the pair kernel has (128, 192, 256: b10c128, small-nbt, wide-nbt) and on ragged batches
-whose last 256-row pair tile is mostly past the batch's rows. Tolerance: the f16 tier's 2e-2 (north_star)."""
+"""The CTA-pair GEMM (the default for one- and two-segment convolutions and token linears) against the one-CTA GEMM
+(KATAGO_CUDA_PAIR=0), the pair kernel without A windows (KATAGO_CUDA_PAIR_WIN=0) and the float64 oracle: the
+trunk's tile widths (128, 192, 256: b10c128, small-nbt, wide-nbt) on ragged batches whose last 256-row pair tile is
+mostly past the batch's rows, and the transformer's token linears (fused RoPE, SwiGLU, masked accumulators, the
+float32 residual stream of the bf16 tier). Tolerance: the f16 tier's 2e-2 (north_star)."""
 
 import os
 
@@ -18,7 +19,7 @@ KEYS = ("policy", "value", "scorevalue", "ownership")
 TOL = 2e-2
 
 
-def forward(name, env, spatial, glob):
+def forward(name, env, spatial, glob, meta=None, prec=kc.PRECISION_F16):
     """A fresh plan built under `env` (the GEMM selection is read when the plan is built)."""
     saved = {k: os.environ.get(k) for k in ("KATAGO_CUDA_PAIR", "KATAGO_CUDA_PAIR_WIN")}
     try:
@@ -26,8 +27,8 @@ def forward(name, env, spatial, glob):
             os.environ.pop(k, None)
         os.environ.update(env)
         m = kc.Model(netgen.net_bytes(name))
-        h = kc.Handle(kc.Context(m, gpu_idxs=[0], precision=kc.PRECISION_F16), max_batch=len(spatial), gpu_idx=0)
-        return h.forward(spatial, glob)
+        h = kc.Handle(kc.Context(m, gpu_idxs=[0], precision=prec), max_batch=len(spatial), gpu_idx=0)
+        return h.forward(spatial, glob, meta)
     finally:
         for k, v in saved.items():
             if v is None:
@@ -51,3 +52,34 @@ def test_pair_gemm_matches_one_cta_gemm_and_oracle(name, batch):
         assert max(errs.values()) <= TOL, (label, errs)
     diff = {k: float(np.abs(runs["pair"][k] - runs["one-CTA"][k]).max()) for k in KEYS}
     assert max(diff.values()) <= TOL, diff
+
+
+# bf16 keeps 8 significant bits: on these random-init transformer nets either GEMM kernel's bf16 outputs sit
+# 0.013-0.023 from the float64 oracle (policy logits up to |3|), and two bf16 runs that differ only in f32
+# accumulation order differ by as much (the roundings diverge), so at bf16 each kernel is held to 3e-2 of the oracle.
+TOL_BF16_NET = 3e-2
+
+
+@pytest.mark.parametrize("name", ["gqa-tf", "small-tf"])
+@pytest.mark.parametrize("prec", [kc.PRECISION_F16, kc.PRECISION_BF16])
+def test_pair_token_linears(name, prec):
+    """The transformer's token linears on the pair kernel (the Q|K|V linear with fused RoPE, the SwiGLU linear, the
+    output linears with a masked accumulator and, at bf16, the float32 residual stream) and on the one-CTA kernel,
+    against the float64 oracle; at f16 also against each other."""
+    batch = 13
+    m = kc.Model(netgen.net_bytes(name))
+    spatial, glob, meta, _ = inputs.synthetic_inputs(batch, 5000 + batch, (9, 13, 19), m.desc.num_input_channels,
+                                                     m.desc.num_input_global_channels,
+                                                     m.desc.num_input_meta_channels, rich=True)
+    want = OracleNet(netgen.net_bytes(name)).forward(spatial, glob, meta, double=True)
+    runs = {"pair": forward(name, {}, spatial, glob, meta, prec),
+            "one-CTA": forward(name, {"KATAGO_CUDA_PAIR": "0"}, spatial, glob, meta, prec)}
+    tol = TOL if prec == kc.PRECISION_F16 else TOL_BF16_NET
+    for label, got in runs.items():
+        for k in KEYS:
+            assert np.all(np.isfinite(got[k])), (label, k)
+        errs = {k: float(np.abs(got[k] - want[k]).max()) for k in KEYS}
+        assert max(errs.values()) <= tol, (label, errs)
+    if prec == kc.PRECISION_F16:
+        diff = {k: float(np.abs(runs["pair"][k] - runs["one-CTA"][k]).max()) for k in KEYS}
+        assert max(diff.values()) <= TOL, diff
