@@ -205,6 +205,7 @@ __global__ void __launch_bounds__(AttnCfg::THREADS, 1)
     const int qrow = t * 128 + r;  // query row within the board
     // the quarter's warps whose 32 rows are all past the board's 400 rows only keep the barrier protocol
     const bool live = t * 128 + q * 32 < 400;
+    const float mq = qrow < 400 ? __ldg(p.rowmask + row0 + qrow) : 0.0f;  // for the output, loaded early
     ok = ok && mbar_wait(s_full, ph, p.err, DEV_TIMEOUT_EPILOGUE);
     __syncwarp();
     tc_fence_after();
@@ -313,7 +314,6 @@ __global__ void __launch_bounds__(AttnCfg::THREADS, 1)
       tmem_ld16(trow + C::O_COL + kq * 16, o);
       tmem_wait_ld();
       if (qrow < 400) {
-        const float mq = p.rowmask[row0 + qrow];
         const float inv = total > 0.0f ? mq / total : 0.0f;
         T* dst = reinterpret_cast<T*>(p.out) + (size_t)(row0 + qrow) * p.out_ld + h * 64 + kq * 16;
 #pragma unroll

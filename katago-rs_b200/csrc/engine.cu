@@ -469,6 +469,10 @@ struct Builder {
     const float* rope_cos = nullptr;
     const float* rope_sin = nullptr;
     int rope_table_stride = 0, rope_q_cols = 0, rope_rot_cols = 0, head_dim = 0, rope_group = 1;
+    // the same tables indexed by board row for the pair kernel: [tables][432][head_dim / 2], rows 400..431
+    // repeating rows 0..31, halo rows zero
+    const float* rope_cos_rows = nullptr;
+    const float* rope_sin_rows = nullptr;
   };
 
   // Tile width of the CTA-pair kernel for this GEMM, or 0 when the one-CTA kernel must run it; `f32` is set for
@@ -668,6 +672,11 @@ struct Builder {
         pm.act = box(act);
         const int kind = s.mode == MODE_ROPE ? PAIR_ROPE : s.mode == MODE_SWIGLU ? PAIR_SWIGLU : pf32 ? PAIR_F32
                          : pwin ? PAIR_WIN : PAIR_SEG;
+        if (kind == PAIR_ROPE) {
+          p.rope_cos = s.rope_cos_rows;
+          p.rope_sin = s.rope_sin_rows;
+          p.rope_table_stride = s.rope_table_stride ? 432 * (s.head_dim / 2) : 0;
+        }
         const int max_pairs = launch_pair<T>(true, pbn, kind, 0, 0, pm, p);
         add(s.cls, [=](cudaStream_t st, int n) {
           GemmParams q = p;
@@ -946,12 +955,27 @@ struct Builder {
     }
     const float* dcos = nullptr;
     const float* dsin = nullptr;
+    const float* dcos_rows = nullptr;
+    const float* dsin_rows = nullptr;
     int tables = 1;
     if (b.use_rope) {
       std::vector<float> cs, sn;
       rope_tables(b, cs, sn, tables);
       dcos = up(cs);
       dsin = up(sn);
+      // board-row-indexed copies (the pair kernel's RoPE epilogue loads 32 consecutive rows per warp)
+      const int half = hd / 2;
+      std::vector<float> cr((size_t)tables * 432 * half, 0.0f), sr(cr.size(), 0.0f);
+      for (int t = 0; t < tables; t++)
+        for (int pr = 0; pr < 432; pr++) {
+          const int rr = pr % 400, y = rr / 20 - 1, x = rr % 20;
+          if (y < 0 || y >= 19 || x >= 19) continue;
+          const size_t src = ((size_t)t * 361 + y * 19 + x) * half, dst = ((size_t)t * 432 + pr) * half;
+          std::copy(cs.begin() + src, cs.begin() + src + half, cr.begin() + dst);
+          std::copy(sn.begin() + src, sn.begin() + src + half, sr.begin() + dst);
+        }
+      dcos_rows = up(cr);
+      dsin_rows = up(sr);
     }
     const int tstride = b.use_rope && b.learnable_rope ? 361 * (hd / 2) : 0;
     const bool fuse_rope = tc && b.use_rope && hd % 32 == 0 && pick_bn(N, 2 * hd) != 0;
@@ -963,6 +987,8 @@ struct Builder {
       s.segs = {g};
       s.rope_cos = dcos;
       s.rope_sin = dsin;
+      s.rope_cos_rows = dcos_rows;
+      s.rope_sin_rows = dsin_rows;
       s.rope_table_stride = tstride;
       s.rope_q_cols = qc;
       s.rope_rot_cols = qc + kc;

@@ -9,7 +9,8 @@
 //    residual and the raw output are float32 (the bf16 tier's residual stream; transformer_attention_block and
 //    transformer_ffn_block's output linears, :1359-1438, with the branch output masked before the add);
 //  * MODE_ROPE: the attention block's Q|K|V linear with 2D RoPE on the Q and K heads (head dim 64, the head's two
-//    rotation halves at columns [0, 32) and [32, 64), :1369-1374 and :449-484): one head per epilogue warp;
+//    rotation halves at columns [0, 32) and [32, 64), :1369-1374 and :449-484): one head per epilogue warp; the
+//    cos / sin tables indexed by board row (GemmParams::rope_cos / rope_sin: [tables][432][32]);
 //  * MODE_SWIGLU: the FFN's first linear and gate, SiLU(x W1) * (x Wg) * mask (:1425-1438), each tile's columns
 //    [linear1 | gate] halves.
 //
@@ -487,6 +488,29 @@ __global__ void __launch_bounds__(PairCfg<BN, WIN, RF32>::THREADS, 1)
       const int r = mrow + lane;
       const float m = r < p.g.rows ? __ldg(p.g.rowmask + r) : 0.0f;
       const int ncol0 = (tile % n_tiles) * BN + h * C::WARP_COLS;
+      // RoPE: this warp's 32 rows of the head's cos / sin table (board-row-indexed, 432 rows per table so that 32
+      // rows from any board row stay inside it), 4 KB blocks read with coalesced 128-bit loads while the
+      // accumulator is computed, into shared memory (the residual ring, unused here) as 128-byte rows with the
+      // 128-byte swizzle, from where each thread reads its row
+      bool rot = false;
+      uint8_t* tab = wbuf + RES_OFF;
+      if constexpr (MODE == MODE_ROPE) {
+        rot = ncol0 < p.rope_rot_cols;
+        if (rot) {
+          const int head = ncol0 / 64;
+          const int table = ncol0 < p.rope_q_cols ? head / p.rope_group : head - p.rope_q_cols / 64;
+          const size_t toff = (size_t)table * p.rope_table_stride + (size_t)(mrow % 400) * 32 + lane * 4;
+#pragma unroll
+          for (int i = 0; i < 8; i++) {
+            const float4 c = __ldg(reinterpret_cast<const float4*>(p.rope_cos + toff + i * 128));
+            const float4 sn = __ldg(reinterpret_cast<const float4*>(p.rope_sin + toff + i * 128));
+            const int row = (lane >> 3) + 4 * i, chunk = lane & 7;
+            const uint32_t off = row * 128 + ((chunk ^ (row & 7)) << 4);
+            *reinterpret_cast<float4*>(tab + off) = c;
+            *reinterpret_cast<float4*>(tab + 4096 + off) = sn;
+          }
+        }
+      }
       if (!mbar_wait(&tfull[acc], acc_phase, p.err, DEV_TIMEOUT_EPILOGUE) || *abort_flag) {
         *abort_flag = 1;
         ok = false;
@@ -591,13 +615,7 @@ __global__ void __launch_bounds__(PairCfg<BN, WIN, RF32>::THREADS, 1)
         }
       } else if constexpr (MODE == MODE_ROPE) {
         // one head of 64 columns per warp: Q and K heads rotated in halves of 32 (x0 at [0, 32), x1 at [32, 64)),
-        // V heads as they are; cos / sin of this row's board point from the head's table (L2-resident)
-        const int rr = r % 400, py = rr / 20 - 1, px = rr % 20;
-        const int pos = py >= 0 && py < 19 && px < 19 ? py * 19 + px : 0;
-        const bool rot = ncol0 < p.rope_rot_cols;
-        const int head = ncol0 / 64;
-        const int table = ncol0 < p.rope_q_cols ? head / p.rope_group : head - p.rope_q_cols / 64;
-        const size_t toff = (size_t)table * p.rope_table_stride + (size_t)pos * 32;
+        // V heads as they are (the table rows were staged above; __syncwarp below orders them before the reads)
         const uint32_t tacc = tmem_base + acc * C::ACC_COLS + ((uint32_t)(q * 32) << 16) + h * C::WARP_COLS;
         uint32_t x0[32], x1[32];
         tmem_ld32(tacc, x0);
@@ -611,8 +629,9 @@ __global__ void __launch_bounds__(PairCfg<BN, WIN, RF32>::THREADS, 1)
         for (int j = 0; j < 32; j += 4) {
           float4 cs = make_float4(1.0f, 1.0f, 1.0f, 1.0f), sn = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
           if (rot) {
-            cs = __ldg(reinterpret_cast<const float4*>(p.rope_cos + toff + j));
-            sn = __ldg(reinterpret_cast<const float4*>(p.rope_sin + toff + j));
+            const uint32_t off = lane * 128 + (((j >> 2) ^ (lane & 7)) << 4);
+            cs = *reinterpret_cast<const float4*>(tab + off);
+            sn = *reinterpret_cast<const float4*>(tab + 4096 + off);
           }
           const float c4[4] = {cs.x, cs.y, cs.z, cs.w}, s4[4] = {sn.x, sn.y, sn.z, sn.w};
 #pragma unroll
