@@ -207,6 +207,7 @@ __global__ void __launch_bounds__(PairCfg<BN, WIN, RF32>::THREADS, 1)
                      const __grid_constant__ CUtensorMap tmAct, const __grid_constant__ GemmParams p) {
   using C = PairCfg<BN, WIN, RF32>;
   static_assert(MODE != MODE_ROPE || C::WARP_COLS == 64, "RoPE tiles give each epilogue warp one head of 64");
+  static_assert(MODE != MODE_ROPE || C::NRES * C::RBOX_BYTES >= 8192, "RoPE table rows (cos + sin) in the ring");
   static_assert(MODE != MODE_SWIGLU || (BN % 128 == 0 && C::EPI_WARPS == 8), "SwiGLU tile halves");
   static_assert(MODE == MODE_SEGMENTS || (!WIN && !RF32), "RoPE / SwiGLU tiles are linears");
   constexpr int fmt = std::is_same<T, __nv_bfloat16>::value ? 1 : 0;
