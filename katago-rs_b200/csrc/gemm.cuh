@@ -9,14 +9,18 @@
 // A is NHWC with one row per point of a 20-column grid per board (19 board columns + 1 zero column shared by the
 // left and right halo) and 20 rows per board (a zero row shared by the boards above and below), so a 3x3 tap is a
 // constant row offset dy*20+dx and the whole convolution is nine shifted row windows of the same tensor: no
-// im2col, no gather. Zero halo rows are maintained by every epilogue (it writes 0 there). The stem reads a
-// 21-column / 2-halo layout built for 5x5 kernels and its epilogue remaps rows into the PBL.
+// gather. Zero halo rows are maintained by every epilogue (it writes 0 there). The stem's 5x5 / 3x3 taps over the
+// 22 input planes are either a one-tap GEMM over an im2col operand in the PBL (tensor-core tiers, built by
+// prep_im2col_kernel) or, in the float32 tier, taps over a 21-column / 2-halo layout whose epilogue remaps rows
+// into the PBL.
 //
-// Two kernels share the epilogue:
-//  * gemm_tc_kernel (f16 / bf16): persistent, warp-specialised tcgen05 kernel. Warp 0 issues TMA loads of the
-//    A window (128 rows x 64 channels at the tap's row offset) and the weight tile into a STAGES-deep ring,
-//    warp 1 issues tcgen05.mma (M = 128, N = BN, K = 16) into one of two TMEM accumulators, warps 2-5 drain the
-//    other accumulator (tcgen05.ld) through the fused epilogue while the next tile's MMAs run.
+// Kernels sharing this file's epilogue:
+//  * gemm_tc_kernel (f16 / bf16): persistent, warp-specialised one-CTA tcgen05 kernel. Warp 0 issues TMA loads of
+//    the A window (128 rows x 64 channels at the tap's row offset) and the weight tile into a STAGES-deep ring,
+//    warp 1 issues tcgen05.mma (M = 128, N = BN, K = 16) into one of two TMEM accumulators, warps 2-9 (two per
+//    TMEM lane quarter) drain the other accumulator (tcgen05.ld) through the fused epilogue while the next tile's
+//    MMAs run. Most GEMMs of the tensor-core tiers run on the CTA-pair kernel instead (gemm_pair.cuh); this one
+//    takes the rest (three output segments, float32 outputs with an activation output, narrow RoPE heads).
 //  * gemm_simt_kernel (f32 parity tier, any type): 64 x 64 register-tiled SIMT GEMM over the same row geometry.
 //
 // Fused epilogue (per row r, column c): + per-board bias (stem: global-feature matmul), x mask (transformer
