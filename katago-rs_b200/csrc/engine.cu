@@ -704,11 +704,13 @@ struct Builder {
       p.a_rows = a_rows;
       p.w = up(s.W);
       if (s.mode != MODE_SEGMENTS) fail(KC_ERR_INVALID, "CUDA backend: fused SwiGLU/RoPE needs the tensor-core path");
+      if (s.A.ld % 4 != 0 || s.cin % 16 != 0 || reinterpret_cast<uintptr_t>(s.A.p) % 16 != 0)
+        fail(KC_ERR_INVALID, "CUDA backend: float32 GEMM operand not 16-byte aligned");
       add(s.cls, [=](cudaStream_t st, int n) {
         GemmParams q = p;
         q.g.rows = n * brows;
         dim3 grid((q.g.rows + 63) / 64, (q.n_total + 63) / 64);
-        launch_pdl(gemm_simt_kernel<T>, dim3(grid), dim3(256), 0, st, q);
+        launch_pdl(gemm_simt_kernel<T>, dim3(grid), dim3(SIMT_THREADS), 0, st, q);
       });
     }
   }

@@ -781,59 +781,88 @@ __global__ void __launch_bounds__(TcCfg<BN, WIN>::THREADS, 1)
 }
 
 // ================================================================================================================
-// SIMT kernel (the f32 tier): 64 x 64 tile, 256 threads, 4 x 4 per thread, K chunks of 16
+// SIMT kernel (the f32 tier): 64 x 64 tile, 128 threads, 8 rows x 4 columns per thread, K chunks of 16 channels of
+// one tap, double-buffered in shared memory with the next chunk's 16-byte global loads in flight during the FMAs.
+// Every output sums its K terms in the same order (taps, then channels) whatever its tile: results do not depend on
+// the batch position. Needs lda % 4 == 0 and cin % 16 == 0 (checked by the host).
 // ================================================================================================================
 
+constexpr int SIMT_THREADS = 128;
+
 template <typename T>
-__global__ void __launch_bounds__(256) gemm_simt_kernel(const __grid_constant__ GemmParams p) {
+__global__ void __launch_bounds__(SIMT_THREADS) gemm_simt_kernel(const __grid_constant__ GemmParams p) {
   pdl_wait();
   pdl_trigger();
   static_assert(sizeof(T) == 4, "the SIMT GEMM is the float32 path");
-  __shared__ float As[16][64 + 4];
-  __shared__ float Ws[16][64 + 4];
-  const int tx = threadIdx.x & 15, ty = threadIdx.x >> 4;
+  __shared__ __align__(16) float As[2][16][64 + 4];  // [buffer][k][row]
+  __shared__ __align__(16) float Ws[2][16][64 + 4];  // [buffer][k][column]
+  const int t = threadIdx.x;
+  const int tx = t & 15, ty = t >> 4;  // columns tx * 4 .. + 3, rows ty * 8 .. + 7
   const int m0 = blockIdx.x * 64, n0 = blockIdx.y * 64;
-  const T* A = reinterpret_cast<const T*>(p.a);
-  const T* W = reinterpret_cast<const T*>(p.w);
+  const float* A = reinterpret_cast<const float*>(p.a);
+  const float* W = reinterpret_cast<const float*>(p.w);
   const int K = p.taps * p.cin;
-  float acc[4][4] = {};
-  for (int tap = 0; tap < p.taps; tap++) {
+  const int chunks_per_tap = p.cin / 16;
+  const int nchunks = p.taps * chunks_per_tap;
+  // this thread's two 16-byte loads of each operand per chunk: rows / columns (t >> 2) and (t >> 2) + 32, channels
+  // (t & 3) * 4 .. + 3
+  const int lr = t >> 2, lk = (t & 3) * 4;
+  float4 ra[2], rw[2];
+  auto fetch = [&](int ch) {
+    const int tap = ch / chunks_per_tap;
+    const int c0 = (ch - tap * chunks_per_tap) * 16 + lk;
     const int off = p.tap_off[tap];
-    for (int c0 = 0; c0 < p.cin; c0 += 16) {
-      // A tile: 64 rows x 16 channels; W tile: 64 columns x 16 k
-      for (int i = threadIdx.x; i < 64 * 16; i += 256) {
-        const int rr = i >> 4, kk = i & 15;
-        const int ra = m0 + rr + off;
-        const int cc = c0 + kk;
-        float av = 0.0f;
-        if (ra >= 0 && ra < p.a_rows && cc < p.cin) av = to_f<T>(A[(size_t)ra * p.lda + cc]);
-        As[kk][rr] = av;
-        const int n = n0 + rr;
-        float wv = 0.0f;
-        if (n < p.n_total && cc < p.cin) wv = to_f<T>(W[(size_t)n * K + tap * p.cin + cc]);
-        Ws[kk][rr] = wv;
-      }
-      __syncthreads();
 #pragma unroll
-      for (int kk = 0; kk < 16; kk++) {
-        float a[4], w[4];
-#pragma unroll
-        for (int i = 0; i < 4; i++) a[i] = As[kk][ty * 4 + i];
-#pragma unroll
-        for (int j = 0; j < 4; j++) w[j] = Ws[kk][tx * 4 + j];
-#pragma unroll
-        for (int i = 0; i < 4; i++)
-#pragma unroll
-          for (int j = 0; j < 4; j++) acc[i][j] = fmaf(a[i], w[j], acc[i][j]);
-      }
-      __syncthreads();
+    for (int h = 0; h < 2; h++) {
+      const int row = m0 + lr + 32 * h + off;
+      ra[h] = row >= 0 && row < p.a_rows ? *reinterpret_cast<const float4*>(A + (size_t)row * p.lda + c0)
+                                         : make_float4(0.f, 0.f, 0.f, 0.f);
+      const int n = n0 + lr + 32 * h;
+      rw[h] = n < p.n_total ? *reinterpret_cast<const float4*>(W + (size_t)n * K + tap * p.cin + c0)
+                            : make_float4(0.f, 0.f, 0.f, 0.f);
     }
+  };
+  auto stash = [&](int buf) {
+#pragma unroll
+    for (int h = 0; h < 2; h++) {
+      const int rr = lr + 32 * h;
+      As[buf][lk + 0][rr] = ra[h].x;
+      As[buf][lk + 1][rr] = ra[h].y;
+      As[buf][lk + 2][rr] = ra[h].z;
+      As[buf][lk + 3][rr] = ra[h].w;
+      Ws[buf][lk + 0][rr] = rw[h].x;
+      Ws[buf][lk + 1][rr] = rw[h].y;
+      Ws[buf][lk + 2][rr] = rw[h].z;
+      Ws[buf][lk + 3][rr] = rw[h].w;
+    }
+  };
+  float acc[8][4] = {};
+  fetch(0);
+  stash(0);
+  __syncthreads();
+  for (int ch = 0; ch < nchunks; ch++) {
+    const int buf = ch & 1;
+    if (ch + 1 < nchunks) fetch(ch + 1);
+#pragma unroll
+    for (int kk = 0; kk < 16; kk++) {
+      const float4 a0 = *reinterpret_cast<const float4*>(&As[buf][kk][ty * 8]);
+      const float4 a1 = *reinterpret_cast<const float4*>(&As[buf][kk][ty * 8 + 4]);
+      const float4 w = *reinterpret_cast<const float4*>(&Ws[buf][kk][tx * 4]);
+      const float a[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
+      const float wv[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+      for (int i = 0; i < 8; i++)
+#pragma unroll
+        for (int j = 0; j < 4; j++) acc[i][j] = fmaf(a[i], wv[j], acc[i][j]);
+    }
+    if (ch + 1 < nchunks) stash(buf ^ 1);
+    __syncthreads();
   }
   const int ncol = n0 + tx * 4;
   if (ncol >= p.n_total) return;
 #pragma unroll
-  for (int i = 0; i < 4; i++) {
-    const int r = m0 + ty * 4 + i;
+  for (int i = 0; i < 8; i++) {
+    const int r = m0 + ty * 8 + i;
     const RowInfo ri = row_info(p.g, r);
     float v[4] = {acc[i][0], acc[i][1], acc[i][2], acc[i][3]};
     const EpiSeg& s = seg_of(p, ncol);
