@@ -21,7 +21,7 @@
 //    TMEM lane quarter) drain the other accumulator (tcgen05.ld) through the fused epilogue while the next tile's
 //    MMAs run. Most GEMMs of the tensor-core tiers run on the CTA-pair kernel instead (gemm_pair.cuh); this one
 //    takes the rest (three output segments, float32 outputs with an activation output, narrow RoPE heads).
-//  * gemm_simt_kernel (f32 parity tier, any type): 64 x 64 register-tiled SIMT GEMM over the same row geometry.
+//  * gemm_simt_kernel (f32 parity tier): 64 x 64 register-tiled SIMT GEMM over the same row geometry.
 //
 // Fused epilogue (per row r, column c): + per-board bias (stem: global-feature matmul), x mask (transformer
 // residual branches), + residual, raw output, BN + activation + mask output for the next layer
