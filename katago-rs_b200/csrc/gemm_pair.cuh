@@ -153,10 +153,11 @@ __device__ __forceinline__ f32x2 add2(f32x2 a, f32x2 b) {
   return d;
 }
 
-// mish(t) * m for two elements t = v * s + b, as act_fn<2> (x * n / (n + 2), n = e^2 + 2e, e = exp(min(x, 20)), x
-// itself above 20) but with one MUFU operation per element: 1 / (n + 2) by Newton-Raphson from the integer-
-// subtraction initial estimate of the reciprocal (0x7EF311C3 - bits(d): 5% relative error for the d in [2, 2.4e17]
-// seen here; two steps r <- r (2 - d r) bring it to 7e-6, below the 2-byte outputs' rounding).
+// mish(t) * m for two elements t = v * s + b, as act_fn<2> (x * n / (n + 2), n = e^2 + 2e, e = exp(min(x, 20)))
+// but with one MUFU operation per element: 1 / (n + 2) by Newton-Raphson from the integer-subtraction initial
+// estimate of the reciprocal (0x7EF311C3 - bits(d): 5% relative error for the d in [2, 2.4e17] seen here; two steps
+// r <- r (2 - d r) bring it to 7e-6, below the 2-byte outputs' rounding). Above x = 20, where act_fn<2> returns x,
+// n / (n + 2) evaluates to 1 within that error, so no select is needed.
 __device__ __forceinline__ f32x2 mish2(f32x2 v, f32x2 s, f32x2 b, float m) {
   const f32x2 t = fma2(v, s, b);
   const f32x2 e = {__expf(fminf(t.x, 20.0f)), __expf(fminf(t.y, 20.0f))};
@@ -167,10 +168,7 @@ __device__ __forceinline__ f32x2 mish2(f32x2 v, f32x2 s, f32x2 b, float m) {
   f32x2 r = {__int_as_float(0x7EF311C3 - __float_as_int(d.x)), __int_as_float(0x7EF311C3 - __float_as_int(d.y))};
   r = mul2(r, fma2(nd, r, two));
   r = mul2(r, fma2(nd, r, two));
-  f32x2 y = mul2(mul2(t, mul2(n, r)), f32x2{m, m});
-  if (t.x > 20.0f) y.x = t.x * m;
-  if (t.y > 20.0f) y.y = t.y * m;
-  return y;
+  return mul2(mul2(t, mul2(n, r)), f32x2{m, m});
 }
 
 // act(v * scale + bias) * mask over 32 columns, scale / bias from shared memory (broadcast reads).
@@ -592,7 +590,11 @@ __global__ void __launch_bounds__(PairCfg<BN, WIN, RF32>::THREADS, 1)
           if (cf & EPI_RAW) {
             float o[32];
 #pragma unroll
-            for (int i = 0; i < 32; i++) o[i] = v[i] * m;
+            for (int i = 0; i < 32; i += 2) {
+              const f32x2 y = mul2({v[i], v[i + 1]}, {m, m});
+              o[i] = y.x;
+              o[i + 1] = y.y;
+            }
             if constexpr (RF32) stage_row_f32(st_raw, lane, o);
             else stage_row<T>(st_raw, lane, o);
           }
