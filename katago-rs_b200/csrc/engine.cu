@@ -354,7 +354,7 @@ enum Role : int {
   R_LEVEL0 = 16,  // + 2 * depth (+0 stream, +1 act)
   R_COUNT = 32
 };
-enum FRole : int { F_POOL, F_GBIAS, F_VPOOL, F_V2, F_PASS, F_PIX, F_COUNT };
+enum FRole : int { F_POOL, F_GBIAS, F_VPOOL, F_V2, F_PASS, F_PIX, F_TIPSS, F_COUNT };
 
 template <typename T>
 struct Builder {
@@ -1269,6 +1269,22 @@ struct Builder {
           else
             launch_pdl(rms_rows_kernel<T, T, true>, dim3((rows + 7) / 8), dim3(256), 0, st, (const T*)X.p, X.ld,
                        C / 128, g, bb, act, eps, Ip->rowmask, rows, (T*)XA.p, XA.ld);
+        });
+      } else if (spatial && rms_vec(X, C, XA)) {
+        // spatial tip: row sums of squares, then per row its board's rms and the affine + activation
+        float* tss = fbuffer(F_TIPSS, 400);
+        add(CLS_OTHER, [=](cudaStream_t st, int n) {
+          const int rows = n * 400;
+          const dim3 grid((rows + 7) / 8), block(256);
+          if (X.f32) {
+            launch_pdl(row_sumsq_kernel<float>, grid, block, 0, st, (const float*)X.p, X.ld, C / 128, rows, tss);
+            launch_pdl(tip_spatial_apply_kernel<float, T>, grid, block, 0, st, (const float*)X.p, X.ld, C / 128,
+                       (const float*)tss, Ip->rowmask, Ip->mask_sum, g, bb, act, eps, rows, (T*)XA.p, XA.ld);
+          } else {
+            launch_pdl(row_sumsq_kernel<T>, grid, block, 0, st, (const T*)X.p, X.ld, C / 128, rows, tss);
+            launch_pdl(tip_spatial_apply_kernel<T, T>, grid, block, 0, st, (const T*)X.p, X.ld, C / 128,
+                       (const float*)tss, Ip->rowmask, Ip->mask_sum, g, bb, act, eps, rows, (T*)XA.p, XA.ld);
+          }
         });
       } else {
         add(CLS_OTHER, [=](cudaStream_t st, int n) {

@@ -464,6 +464,76 @@ __global__ void rms_rows_kernel(const TI* __restrict__ x, int ld, int nv, const 
   }
 }
 
+// Spatial trunk-tip RMSNorm (trunk_tip_rmsnorm :1440-1463 with one rms per board over its channels x on-board
+// points) in two row-parallel steps. Step 1: the sum of squares of each PBL row's C = 128 nv channels, one warp per
+// row.
+template <typename TI>
+__global__ void row_sumsq_kernel(const TI* __restrict__ x, int ld, int nv, int rows, float* __restrict__ ss) {
+  pdl_wait();
+  pdl_trigger();
+  const int r = blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
+  const int lane = threadIdx.x & 31;
+  if (r >= rows) return;
+  const TI* xr = x + (size_t)r * ld + lane * 4;
+  float s = 0.0f;
+#pragma unroll
+  for (int i = 0; i < 8; i++) {
+    if (i < nv) {
+      const float4 v = load4<TI>(xr + i * 128);
+      s += v.x * v.x;
+      s += v.y * v.y;
+      s += v.z * v.z;
+      s += v.w * v.w;
+    }
+  }
+  for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+  if (lane == 0) ss[r] = s;
+}
+
+// Step 2, one warp per row: the row's board total of the on-board rows' sums of squares (each warp adds the
+// board's 400 values; they are L2-resident), rms = 1 / sqrt(total / (on-board points x C) + eps), then
+// y = act(x * rms * gamma + beta) * mask as the per-point tip.
+template <typename TI, typename T>
+__global__ void tip_spatial_apply_kernel(const TI* __restrict__ x, int ld, int nv, const float* __restrict__ ss,
+                                         const float* __restrict__ rowmask, const float* __restrict__ mask_sum,
+                                         const float* __restrict__ gamma, const float* __restrict__ beta, int act,
+                                         float eps, int rows, T* __restrict__ y, int yld) {
+  pdl_wait();
+  pdl_trigger();
+  const int r = blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
+  const int lane = threadIdx.x & 31;
+  if (r >= rows) return;
+  const int b0 = (r / 400) * 400;
+  float t = 0.0f;
+  for (int k = lane; k < 400; k += 32) t += ss[b0 + k] * rowmask[b0 + k];
+  for (int o = 16; o > 0; o >>= 1) t += __shfl_xor_sync(0xffffffffu, t, o);
+  const float count = mask_sum[r / 400] * (float)(nv * 128);
+  const float ms = t / count;
+  const float rms = 1.0f / sqrtf(ms + eps);
+  const float m = rowmask[r];
+  const TI* xr = x + (size_t)r * ld + lane * 4;
+  T* yr = y + (size_t)r * yld + lane * 4;
+#pragma unroll
+  for (int i = 0; i < 8; i++) {
+    if (i < nv) {
+      const int c = i * 128 + lane * 4;
+      const float4 v = load4<TI>(xr + i * 128);
+      const float4 g = __ldg(reinterpret_cast<const float4*>(gamma + c));
+      const float4 bt = __ldg(reinterpret_cast<const float4*>(beta + c));
+      const float xv[4] = {v.x * rms, v.y * rms, v.z * rms, v.w * rms};
+      const float gg[4] = {g.x, g.y, g.z, g.w}, bb[4] = {bt.x, bt.y, bt.z, bt.w};
+      float o[4];
+#pragma unroll
+      for (int k = 0; k < 4; k++) {
+        float u = xv[k] * gg[k];
+        u = u + bb[k];
+        o[k] = act_apply(u, act) * m;
+      }
+      store4<T>(yr + i * 128, o[0], o[1], o[2], o[3]);
+    }
+  }
+}
+
 // ---------------------------------------------------------------------------------------------------------------
 // Trunk-tip RMSNorm (bin2onnx.py trunk_tip_rmsnorm :1440-1463): act(x * rms * gamma + beta) * mask, rms per point
 // over channels, or (spatial) one rms per board over channels x on-board points. One block per board.

@@ -210,10 +210,11 @@ def small_tf() -> NetSpec:
 
 def gqa_tf() -> NetSpec:
     """Grouped-query attention at head dim 64 (the tensor-core attention kernel's KV-head mapping): 6 query heads
-    over 2 KV heads, then 4 over 1, fixed-theta RoPE."""
+    over 2 KV heads, then 4 over 1, fixed-theta RoPE; spatial RMSNorm trunk tip at a width of 384 (the row-parallel
+    tip kernels)."""
     blocks: List[Block] = [Attention(heads=6, kv_heads=2, rope="fixed", rope_theta=100.0), FFN(ffn=512),
                            Attention(heads=4, kv_heads=1, rope="learnable"), FFN(ffn=256)]
-    return NetSpec("gqa-tf", 17, 384, blocks, stem_k=3, act=ACT_SILU, tip="rms", policy_channels=2, v2=64)
+    return NetSpec("gqa-tf", 17, 384, blocks, stem_k=3, act=ACT_SILU, tip="rms_spatial", policy_channels=2, v2=64)
 
 
 NETS = {

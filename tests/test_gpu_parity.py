@@ -55,7 +55,7 @@ def test_golden(name, mode):
 
 @pytest.mark.parametrize("name,prec", [("small-nbt", kc.PRECISION_F16), ("tiny-nbt", kc.PRECISION_F32),
                                        ("small-tf", kc.PRECISION_BF16), ("tiny-tf-learn", kc.PRECISION_F32),
-                                       ("tiny-v15-meta", kc.PRECISION_F16)])
+                                       ("tiny-v15-meta", kc.PRECISION_F16), ("gqa-tf", kc.PRECISION_F32)])
 def test_oracle_mixed_boards(name, prec):
     """Batches of mixed 9x9 / 13x13 / 19x19 boards (masked BN, masked pooling and the max-pool paths), larger than one
     128-row tile, against the float32 oracle."""
