@@ -225,6 +225,7 @@ int launch_pair(bool prepare, int bn, int kind, int pairs, cudaStream_t s, const
     case PAIR_F32 * 1000 + 128: return launch_pair_bn<T, 128, false, MODE_SEGMENTS, true>(prepare, pairs, s, m, p);
     case PAIR_F32 * 1000 + 192: return launch_pair_bn<T, 192, false, MODE_SEGMENTS, true>(prepare, pairs, s, m, p);
     case PAIR_ROPE * 1000 + 128: return launch_pair_bn<T, 128, false, MODE_ROPE, false>(prepare, pairs, s, m, p);
+    case PAIR_ROPE * 1000 + 192: return launch_pair_bn<T, 192, false, MODE_ROPE, false>(prepare, pairs, s, m, p);
     case PAIR_SWIGLU * 1000 + 128: return launch_pair_bn<T, 128, false, MODE_SWIGLU, false>(prepare, pairs, s, m, p);
     case PAIR_SWIGLU * 1000 + 256: return launch_pair_bn<T, 256, false, MODE_SWIGLU, false>(prepare, pairs, s, m, p);
     default:
@@ -491,8 +492,11 @@ struct Builder {
       const Seg& g = s.segs[0];
       if (p.nseg != 1 || g.raw.f32 || !aligned(g.raw, g.raw_c0)) return 0;
       if (s.mode == MODE_ROPE) {
-        // 128 columns: two heads, one per epilogue warp of a lane quarter
-        return s.head_dim == 64 && s.N % 128 == 0 ? 128 : 0;
+        // one head of 64 per epilogue warp: 192 columns (three warps per lane quarter) or 128 (two)
+        if (s.head_dim != 64) return 0;
+        for (int bn : {192, 128})
+          if (s.N % bn == 0) return bn;
+        return 0;
       } else {
         for (int bn : {256, 128})
           if (s.N % bn == 0) return bn;

@@ -205,7 +205,8 @@ __global__ void __launch_bounds__(PairCfg<BN, WIN, RF32>::THREADS, 1)
                      const __grid_constant__ CUtensorMap tmAct, const __grid_constant__ GemmParams p) {
   using C = PairCfg<BN, WIN, RF32>;
   static_assert(MODE != MODE_ROPE || C::WARP_COLS == 64, "RoPE tiles give each epilogue warp one head of 64");
-  static_assert(MODE != MODE_ROPE || C::NRES * C::RBOX_BYTES >= 8192, "RoPE table rows (cos + sin) in the ring");
+  static_assert(MODE != MODE_ROPE || (C::NRES * C::RBOX_BYTES >= 4096 && C::RBOX_BYTES + C::ABOX_BYTES == 4096),
+                "RoPE table rows: cos in the residual ring, sin in the raw and act staging boxes");
   static_assert(MODE != MODE_SWIGLU || (BN % 128 == 0 && C::EPI_WARPS == 8), "SwiGLU tile halves");
   static_assert(MODE == MODE_SEGMENTS || (!WIN && !RF32), "RoPE / SwiGLU tiles are linears");
   constexpr int fmt = std::is_same<T, __nv_bfloat16>::value ? 1 : 0;
@@ -489,13 +490,17 @@ __global__ void __launch_bounds__(PairCfg<BN, WIN, RF32>::THREADS, 1)
       const int ncol0 = (tile % n_tiles) * BN + h * C::WARP_COLS;
       // RoPE: this warp's 32 rows of the head's cos / sin table (board-row-indexed, 432 rows per table so that 32
       // rows from any board row stay inside it), 4 KB blocks read with coalesced 128-bit loads while the
-      // accumulator is computed, into shared memory (the residual ring, unused here) as 128-byte rows with the
-      // 128-byte swizzle, from where each thread reads its row
+      // accumulator is computed, into shared memory as 128-byte rows with the 128-byte swizzle, from where each
+      // thread reads its row: cos in the residual ring (unused here), sin in the raw and act staging boxes, free
+      // until this tile's outputs are staged once the previous tile's stores have read them
       bool rot = false;
       uint8_t* tab = wbuf + RES_OFF;
+      uint8_t* tab_s = wbuf;
       if constexpr (MODE == MODE_ROPE) {
         rot = ncol0 < p.rope_rot_cols;
         if (rot) {
+          if (lane == 0) bulk_wait_read0();
+          __syncwarp();
           const int head = ncol0 / 64;
           const int table = ncol0 < p.rope_q_cols ? head / p.rope_group : head - p.rope_q_cols / 64;
           const size_t toff = (size_t)table * p.rope_table_stride + (size_t)(mrow % 400) * 32 + lane * 4;
@@ -506,7 +511,7 @@ __global__ void __launch_bounds__(PairCfg<BN, WIN, RF32>::THREADS, 1)
             const int row = (lane >> 3) + 4 * i, chunk = lane & 7;
             const uint32_t off = row * 128 + ((chunk ^ (row & 7)) << 4);
             *reinterpret_cast<float4*>(tab + off) = c;
-            *reinterpret_cast<float4*>(tab + 4096 + off) = sn;
+            *reinterpret_cast<float4*>(tab_s + off) = sn;
           }
         }
       }
@@ -634,7 +639,7 @@ __global__ void __launch_bounds__(PairCfg<BN, WIN, RF32>::THREADS, 1)
           if (rot) {
             const uint32_t off = lane * 128 + (((j >> 2) ^ (lane & 7)) << 4);
             cs = *reinterpret_cast<const float4*>(tab + off);
-            sn = *reinterpret_cast<const float4*>(tab + 4096 + off);
+            sn = *reinterpret_cast<const float4*>(tab_s + off);
           }
           const float c4[4] = {cs.x, cs.y, cs.z, cs.w}, s4[4] = {sn.x, sn.y, sn.z, sn.w};
 #pragma unroll
