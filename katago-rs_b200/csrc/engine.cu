@@ -216,9 +216,11 @@ template <typename T>
 int launch_pair(bool prepare, int bn, int kind, int pairs, cudaStream_t s, const PairMaps& m, const GemmParams& p) {
   const int key = kind * 1000 + bn;
   switch (key) {
+    case PAIR_SEG * 1000 + 64: return launch_pair_bn<T, 64, false, MODE_SEGMENTS, false>(prepare, pairs, s, m, p);
     case PAIR_SEG * 1000 + 128: return launch_pair_bn<T, 128, false, MODE_SEGMENTS, false>(prepare, pairs, s, m, p);
     case PAIR_SEG * 1000 + 192: return launch_pair_bn<T, 192, false, MODE_SEGMENTS, false>(prepare, pairs, s, m, p);
     case PAIR_SEG * 1000 + 256: return launch_pair_bn<T, 256, false, MODE_SEGMENTS, false>(prepare, pairs, s, m, p);
+    case PAIR_WIN * 1000 + 64: return launch_pair_bn<T, 64, true, MODE_SEGMENTS, false>(prepare, pairs, s, m, p);
     case PAIR_WIN * 1000 + 128: return launch_pair_bn<T, 128, true, MODE_SEGMENTS, false>(prepare, pairs, s, m, p);
     case PAIR_WIN * 1000 + 192: return launch_pair_bn<T, 192, true, MODE_SEGMENTS, false>(prepare, pairs, s, m, p);
     case PAIR_WIN * 1000 + 256: return launch_pair_bn<T, 256, true, MODE_SEGMENTS, false>(prepare, pairs, s, m, p);
@@ -682,10 +684,31 @@ struct Builder {
           p.rope_table_stride = s.rope_table_stride ? 432 * (s.head_dim / 2) : 0;
         }
         const int max_pairs = launch_pair<T>(true, pbn, kind, 0, 0, pm, p);
+        // Small batches: the convolutions also get 64-column tiles (three or six per row tile instead of one or two)
+        // when that spreads a launch over more SM pairs than it adds tile rounds (KATAGO_CUDA_PAIR_NARROW=0: off).
+        // A tile costs about its width plus a fixed ~74 columns' worth (prologue, pipeline fill, epilogue).
+        const char* ne = std::getenv("KATAGO_CUDA_PAIR_NARROW");
+        const bool narrow = (kind == PAIR_SEG || kind == PAIR_WIN) && pbn > 64 && s.N % 64 == 0 && !(ne && ne[0] == '0');
+        PairMaps pm64 = pm;
+        int max_pairs64 = 0;
+        if (narrow) {
+          pm64.b = make_map(dW, bf16, K, s.N, 32);
+          max_pairs64 = launch_pair<T>(true, 64, kind, 0, 0, pm64, p);
+        }
         add(s.cls, [=](cudaStream_t st, int n) {
           GemmParams q = p;
           q.g.rows = n * brows;
-          const int tiles = ((q.g.rows + 255) / 256) * (q.n_total / pbn);
+          const int mt = (q.g.rows + 255) / 256;
+          const int tiles = mt * (q.n_total / pbn);
+          if (narrow) {
+            const int tiles64 = mt * (q.n_total / 64);
+            const long long cost = (long long)((tiles + max_pairs - 1) / max_pairs) * (pbn + 74);
+            const long long cost64 = (long long)((tiles64 + max_pairs64 - 1) / max_pairs64) * (64 + 74);
+            if (cost64 < cost) {
+              launch_pair<T>(false, 64, kind, std::min(tiles64, max_pairs64), st, pm64, q);
+              return;
+            }
+          }
           launch_pair<T>(false, pbn, kind, std::min(tiles, max_pairs), st, pm, q);
         });
         return;
