@@ -490,9 +490,10 @@ __global__ void row_sumsq_kernel(const TI* __restrict__ x, int ld, int nv, int r
   if (lane == 0) ss[r] = s;
 }
 
-// Step 2, one warp per row: the row's board total of the on-board rows' sums of squares (each warp adds the
-// board's 400 values; they are L2-resident), rms = 1 / sqrt(total / (on-board points x C) + eps), then
-// y = act(x * rms * gamma + beta) * mask as the per-point tip.
+// Step 2, one warp per row (8 rows per block of 256 threads): the board total of the on-board rows' sums of squares
+// (each block adds the 400 values of the one or two boards its rows belong to, in the same order for every block),
+// rms = 1 / sqrt(total / (on-board points x C) + eps), then y = act(x * rms * gamma + beta) * mask as the per-point
+// tip.
 template <typename TI, typename T>
 __global__ void tip_spatial_apply_kernel(const TI* __restrict__ x, int ld, int nv, const float* __restrict__ ss,
                                          const float* __restrict__ rowmask, const float* __restrict__ mask_sum,
@@ -500,13 +501,27 @@ __global__ void tip_spatial_apply_kernel(const TI* __restrict__ x, int ld, int n
                                          float eps, int rows, T* __restrict__ y, int yld) {
   pdl_wait();
   pdl_trigger();
-  const int r = blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
-  const int lane = threadIdx.x & 31;
+  __shared__ float part[2][8];
+  const int warp = threadIdx.x / 32, lane = threadIdx.x & 31;
+  const int r = blockIdx.x * 8 + warp;
+  const int bfirst = (blockIdx.x * 8) / 400;
+  const int blast = min(blockIdx.x * 8 + 7, rows - 1) / 400;
+#pragma unroll
+  for (int bi = 0; bi < 2; bi++) {
+    float t = 0.0f;
+    if (bfirst + bi <= blast) {
+      const int b0 = (bfirst + bi) * 400;
+      for (int k = threadIdx.x; k < 400; k += 256) t += ss[b0 + k] * rowmask[b0 + k];
+    }
+    for (int o = 16; o > 0; o >>= 1) t += __shfl_xor_sync(0xffffffffu, t, o);
+    if (lane == 0) part[bi][warp] = t;
+  }
+  __syncthreads();
   if (r >= rows) return;
-  const int b0 = (r / 400) * 400;
+  const int bi = r / 400 - bfirst;
   float t = 0.0f;
-  for (int k = lane; k < 400; k += 32) t += ss[b0 + k] * rowmask[b0 + k];
-  for (int o = 16; o > 0; o >>= 1) t += __shfl_xor_sync(0xffffffffu, t, o);
+#pragma unroll
+  for (int w = 0; w < 8; w++) t += part[bi][w];
   const float count = mask_sum[r / 400] * (float)(nv * 128);
   const float ms = t / count;
   const float rms = 1.0f / sqrtf(ms + eps);
