@@ -628,13 +628,51 @@ __global__ void head_spatial_kernel(const T* __restrict__ p1a, int p1ld, int p1c
   int b = idx / 361, pos = idx - b * 361;
   int r = pbl_row(b, pos / 19, pos % 19);
   float* o = out + (size_t)b * row_len;
-  for (int p = 0; p < P; p++) {
-    float a = 0.0f;
-    for (int c = 0; c < p1c; c++) a += to_f<T>(p1a[(size_t)r * p1ld + c]) * __ldg(w2 + (size_t)c * P + p);
-    o[p * 362 + pos] = a;
+  constexpr int VW = 16 / (int)sizeof(T);  // elements per 16-byte vector
+  const T* pr = p1a + (size_t)r * p1ld;
+  if (P <= 4 && p1ld % VW == 0) {
+    // the row's channels as 16-byte vectors, all (up to 4) policy outputs at once; each output still sums its
+    // channels in order
+    float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+    int c = 0;
+    for (; c + VW <= p1c; c += VW) {
+      const uint4 u = *reinterpret_cast<const uint4*>(pr + c);
+      const T* e = reinterpret_cast<const T*>(&u);
+#pragma unroll
+      for (int k = 0; k < VW; k++) {
+        const float a = to_f<T>(e[k]);
+#pragma unroll
+        for (int p = 0; p < 4; p++)
+          if (p < P) acc[p] += a * __ldg(w2 + (size_t)(c + k) * P + p);
+      }
+    }
+    for (; c < p1c; c++) {
+      const float a = to_f<T>(pr[c]);
+#pragma unroll
+      for (int p = 0; p < 4; p++)
+        if (p < P) acc[p] += a * __ldg(w2 + (size_t)c * P + p);
+    }
+#pragma unroll
+    for (int p = 0; p < 4; p++)
+      if (p < P) o[p * 362 + pos] = acc[p];
+  } else {
+    for (int p = 0; p < P; p++) {
+      float a = 0.0f;
+      for (int c = 0; c < p1c; c++) a += to_f<T>(pr[c]) * __ldg(w2 + (size_t)c * P + p);
+      o[p * 362 + pos] = a;
+    }
   }
+  const T* vr = v1a + (size_t)r * v1ld + v1c0;
   float a = 0.0f;
-  for (int c = 0; c < v1c; c++) a += to_f<T>(v1a[(size_t)r * v1ld + v1c0 + c]) * __ldg(wown + c);
+  int c = 0;
+  if (v1ld % VW == 0 && v1c0 % VW == 0)
+    for (; c + VW <= v1c; c += VW) {
+      const uint4 u = *reinterpret_cast<const uint4*>(vr + c);
+      const T* e = reinterpret_cast<const T*>(&u);
+#pragma unroll
+      for (int k = 0; k < VW; k++) a += to_f<T>(e[k]) * __ldg(wown + c + k);
+    }
+  for (; c < v1c; c++) a += to_f<T>(vr[c]) * __ldg(wown + c);
   o[own_off + pos] = a;
 }
 
