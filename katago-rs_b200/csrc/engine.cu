@@ -817,7 +817,9 @@ struct Builder {
     const float* sc = up(bn.merged_scale);
     const float* bi = up(bn.merged_bias);
     Engine::Impl* Ip = &I;
-    const int Cw = y.ld;
+    // written width: the channels plus the zero padding a consumer GEMM reads (its input channels are padded to a
+    // multiple of 64), not the whole row of the shared buffer
+    const int Cw = std::min(y.ld, round_up(C, 64));
     if (xc0 % 8 != 0 || x.ld % 8 != 0 || Cw % 8 != 0)
       fail(KC_ERR_INVALID, "CUDA backend: biased batch-norm pass on unaligned channels");
     add(CLS_OTHER, [=](cudaStream_t st, int n) {
