@@ -8,10 +8,15 @@ crates/katago-nn-burn/examples/bench.rs:27-32: plane 0 = mask, stones at ~30%, g
     python bench.py [--gpus N --steps K --warmup W] [--impl reference]
 
 Our arm prints one JSON line with `value` (device-resident inputs, CUDA events on the handle's stream, L2 flushed
-between timed steps), `e2e` (the same through the C ABI's host path kc_enqueue / kc_wait: pinned-host inputs copied
-in and output rows copied back every step), the roofline of the dominant kernel class (the 3x3-conv CTA-pair tcgen05 GEMM)
-and a CPU baseline (the CPU oracle, rank 0 at N = 1). Under torchrun each rank drives its own GPU with its own
-batch (weak scaling, no collective on the data path); the time is the max over ranks.
+between timed steps), `e2e` (the same through the C ABI's host path kc_enqueue / kc_wait, timed by the host clock:
+pinned-host inputs copied in and every output row copied back each step), the roofline of the dominant kernel class
+(the 3x3-conv CTA-pair tcgen05 GEMM) and a CPU baseline (the CPU oracle, rank 0 at N = 1). Under torchrun each rank
+drives its own GPU with its own batch (weak scaling, no collective on the data path); the time is the max over
+ranks. `--in-process` runs the N GPUs as N handles of one process, one host thread each (katago-rs's own layout:
+one NN server thread per GPU), and takes the max over the threads.
+
+`--boards 9,13,19` draws each position's board size from the list (the mixed-board configuration, padded into
+19x19 under the on-board mask).
 
 `--impl reference` times the reference path on the host CPU cores: the reference's `flex` backend needs cargo and
 cannot be built here, so its arithmetic is timed through the CPU restatement in oracle/ (kind "port").
@@ -27,21 +32,36 @@ import subprocess
 import sys
 import time
 
+import numpy as np
+
 REPO = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, os.path.join(REPO, "katago-rs_b200", "python"))
 
 METRIC = "b18c384nbt evals/s at batch 256 per GPU"
+UNIT = "evals/s"
+# DRAM bytes (read + write) per launch of the 3x3-convolution GEMM, from an ncu capture of this benchmark's own
+# kernel (`--metrics dram__bytes_read.sum,dram__bytes_write.sum`): one line per workload, "net batch boards bytes".
+TRAFFIC_FILE = os.path.join(REPO, "profiles", "conv3x3_dram_bytes_per_launch.txt")
 
 
 def metric_name(args):
-    """The headline metric, or the same metric for another --net / --batch (a parity or exploration run)."""
-    if args.net == "b18c384nbt" and args.batch == 256:
+    """The headline metric, or the same metric for another --net / --batch / --boards (a parity, mixed-board or
+    exploration run)."""
+    if args.net == "b18c384nbt" and args.batch == 256 and args.boards == "19":
         return METRIC
-    return f"{args.net} evals/s at batch {args.batch} per GPU"
-UNIT = "evals/s"
-# DRAM bytes (read + write) per 3x3-convolution GEMM launch at batch 256, from the full ncu capture summarised in
-# profiles/gemm_pair_b18c384nbt_batch256.md (mean of the two 3x3 launches captured).
-CONV3_DRAM_BYTES_PER_LAUNCH = 75.0e6
+    on = "" if args.boards == "19" else f" on {args.boards.replace(',', '/')} boards"
+    return f"{args.net} evals/s at batch {args.batch} per GPU{on}"
+
+
+def conv3_traffic(args):
+    try:
+        for line in open(TRAFFIC_FILE):
+            f = line.split()
+            if len(f) == 4 and not line.startswith("#") and f[:3] == [args.net, str(args.batch), args.boards]:
+                return float(f[3])
+    except OSError:
+        pass
+    return None
 
 
 def parse():
@@ -52,7 +72,11 @@ def parse():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--net", default="b18c384nbt")
     ap.add_argument("--batch", type=int, default=256)
+    ap.add_argument("--boards", default="19", help="board sizes drawn uniformly per position, e.g. 9,13,19")
     ap.add_argument("--precision", default="f16", choices=["f16", "bf16", "f32"])
+    ap.add_argument("--in-process", action="store_true",
+                    help="--gpus N handles in this one process, one host thread per GPU (katago-rs's NN server "
+                         "threads) instead of one process per GPU under torchrun")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
     return ap.parse_args()
@@ -80,7 +104,8 @@ def reduce_timing(total_ms, rows_per_rank, steps, dist=None, device=None):
 
 def workload(args, rank):
     from katago_cuda import inputs
-    return inputs.synthetic_inputs(args.batch, 0xB200 + rank, (19,))
+    sizes = tuple(int(x) for x in args.boards.split(","))
+    return inputs.synthetic_inputs(args.batch, 0xB200 + rank, sizes)
 
 
 def peaks():
@@ -255,107 +280,172 @@ def run_reference(args):
     print(json.dumps(line), flush=True)
 
 
+class Runner:
+    """One compute handle on one GPU with its benchmark batch: device-resident copies of the inputs (for `value`),
+    the handle's pinned staging buffers (for `e2e`), and the L2 flush buffer."""
+
+    def __init__(self, args, ctx, gpu, seed_rank):
+        import torch
+
+        import katago_cuda as kc
+        self.args = args
+        self.gpu = gpu
+        self.dev = torch.device("cuda", gpu)
+        self.h = kc.Handle(ctx, max_batch=args.batch, gpu_idx=gpu)
+        self.spatial, self.glob, _, _ = workload(args, seed_rank)
+        with torch.cuda.device(self.dev):
+            self.d_sp = torch.from_numpy(self.spatial).to(self.dev)
+            self.d_gl = torch.from_numpy(self.glob).to(self.dev)
+            self.d_out = torch.zeros((args.batch, self.h.row_len), dtype=torch.float32, device=self.dev)
+            self.stream = torch.cuda.ExternalStream(self.h.stream_ptr(), device=self.dev)
+            self.flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device=self.dev)  # > 126 MB L2
+
+    def step(self):
+        self.h.enqueue_device(self.args.batch, self.d_sp.data_ptr(), self.d_gl.data_ptr(), 0, self.d_out.data_ptr())
+
+    def _flush(self):
+        import torch
+        with torch.cuda.device(self.dev), torch.cuda.stream(self.stream):
+            self.flush.zero_()
+
+    def warm(self):
+        """Both CUDA graphs (plain, and with per-launch timing events) are captured here."""
+        n = max(3, self.args.warmup)
+        self.h.set_profiling(True)
+        for _ in range(n):
+            self.step()
+            self.h.synchronize()
+        self.h.set_profiling(False)
+        for _ in range(n):
+            self.step()
+            self.h.synchronize()
+        self.h.spatial[:self.args.batch] = self.spatial
+        self.h.glob[:self.args.batch] = self.glob
+        for _ in range(n):
+            self.h.enqueue(self.args.batch)
+            self.h.wait()
+
+    def timed(self, k, profiled):
+        """k steps on the handle's stream, each bracketed by CUDA events on that stream, L2 flushed before each
+        (outside the events). Returns (total ms, per-class profile or None)."""
+        import torch
+        with torch.cuda.device(self.dev):
+            ev_s = [torch.cuda.Event(enable_timing=True) for _ in range(k)]
+            ev_e = [torch.cuda.Event(enable_timing=True) for _ in range(k)]
+            if profiled:
+                self.h.set_profiling(True)  # resets the per-class accumulators
+            for i in range(k):
+                self._flush()
+                ev_s[i].record(self.stream)
+                self.h.enqueue_device(self.args.batch, self.d_sp.data_ptr(), self.d_gl.data_ptr(), 0,
+                                      self.d_out.data_ptr())
+                ev_e[i].record(self.stream)
+                self.h.synchronize()
+            prof = self.h.profile() if profiled else None
+            if profiled:
+                self.h.set_profiling(False)
+            return sum(ev_s[i].elapsed_time(ev_e[i]) for i in range(k)), prof
+
+    def timed_e2e(self, k):
+        """k steps through the C ABI host path, timed by the host clock around kc_enqueue + kc_wait: the copy of
+        the pinned inputs to the device, the forward pass and the copy of every output row back, plus the host
+        side of both calls. L2 flushed before each step, outside the timed region."""
+        import torch
+        total = 0.0
+        for _ in range(k):
+            self._flush()
+            with torch.cuda.device(self.dev):
+                self.stream.synchronize()
+            t0 = time.perf_counter()
+            self.h.enqueue(self.args.batch)
+            rows = self.h.wait()
+            total += time.perf_counter() - t0
+            if not np.isfinite(rows[0, 0]):
+                raise RuntimeError("non-finite output in the e2e run")
+        return 1e3 * total
+
+    def check_outputs(self):
+        out = self.d_out.cpu().numpy()
+        if not np.all(np.isfinite(out)):
+            raise RuntimeError("non-finite outputs in the timed run")
+
+
 def run_ours(args):
-    import numpy as np
     import torch
 
     import katago_cuda as kc
     from katago_cuda import netgen
 
     rank, world, local = dist_env()
-    torch.cuda.set_device(local)
     dist = None
     if world > 1:
         import datetime
 
         import torch.distributed as dist
+        torch.cuda.set_device(local)
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=180), device_id=torch.device("cuda", local))
+    in_process = args.in_process and world == 1 and args.gpus > 1
+    gpus = list(range(args.gpus)) if in_process else [local]
+    torch.cuda.set_device(gpus[0])
 
     prec = {"f16": kc.PRECISION_F16, "bf16": kc.PRECISION_BF16, "f32": kc.PRECISION_F32}[args.precision]
     model = kc.Model(netgen.net_bytes(args.net))
-    ctx = kc.Context(model, gpu_idxs=[local], precision=prec)
-    h = kc.Handle(ctx, max_batch=args.batch, gpu_idx=local)
+    ctx = kc.Context(model, gpu_idxs=gpus, precision=prec)
     flops_row, conv3_row = model.flops()
+    runners = [Runner(args, ctx, g, rank if not in_process else g) for g in gpus]
 
-    spatial, glob, meta, _ = workload(args, rank)
-    dev = torch.device("cuda", local)
-    d_sp = torch.from_numpy(spatial).to(dev)
-    d_gl = torch.from_numpy(glob).to(dev)
-    d_out = torch.zeros((args.batch, h.row_len), dtype=torch.float32, device=dev)
-    stream = torch.cuda.ExternalStream(h.stream_ptr(), device=dev)
-    flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device=dev)  # > 126 MB L2
+    def each(fn):
+        """fn(runner) on every runner, one host thread per GPU when there are several (katago-rs's NN server
+        threads), started together."""
+        if len(runners) == 1:
+            return [fn(runners[0])]
+        import threading
+        res = [None] * len(runners)
+        err = []
+        gate = threading.Barrier(len(runners))
 
-    def step():
-        h.enqueue_device(args.batch, d_sp.data_ptr(), d_gl.data_ptr(), 0, d_out.data_ptr())
+        def go(i):
+            try:
+                torch.cuda.set_device(runners[i].gpu)
+                gate.wait()
+                res[i] = fn(runners[i])
+            except Exception as e:  # noqa: BLE001
+                err.append(e)
+        ts = [threading.Thread(target=go, args=(i,)) for i in range(len(runners))]
+        for t in ts:
+            t.start()
+        for t in ts:
+            t.join()
+        if err:
+            raise err[0]
+        return res
 
-    def timed(k, profiled):
-        """k steps on the handle's stream, each bracketed by CUDA events, L2 flushed before each (untimed)."""
-        ev_s = [torch.cuda.Event(enable_timing=True) for _ in range(k)]
-        ev_e = [torch.cuda.Event(enable_timing=True) for _ in range(k)]
-        if profiled:
-            h.set_profiling(True)  # resets the per-class accumulators
-        for i in range(k):
-            with torch.cuda.stream(stream):
-                flush.zero_()
-                ev_s[i].record(stream)
-            step()
-            ev_e[i].record(stream)
-        stream.synchronize()
-        h.synchronize()
-        prof = h.profile() if profiled else None
-        return sum(ev_s[i].elapsed_time(ev_e[i]) for i in range(k)), prof
-
-    # warm-up: both CUDA graphs (plain, and with per-launch timing events) are captured here
-    h.set_profiling(True)
-    for _ in range(max(3, args.warmup)):
-        step()
-    h.synchronize()
-    h.set_profiling(False)
-    for _ in range(max(3, args.warmup)):
-        step()
-    h.synchronize()
-    launches_per_step = h.launch_count(args.batch)
+    each(lambda r: r.warm())
+    launches_per_step = runners[0].h.launch_count(args.batch)
 
     if dist:
         dist.barrier()
-    torch.cuda.synchronize()
-    clocks = ClockSampler(local, dev)
+    for g in gpus:
+        torch.cuda.synchronize(g)
+    clocks = ClockSampler(gpus[0], torch.device("cuda", gpus[0]))
     clocks.start()
     # headline: the plain graph; then the same K steps again with an event pair around every launch, which gives
     # the per-kernel-class device times (the events cost a few percent, so they stay out of the headline)
-    total_ms, _ = timed(args.steps, False)
-    prof_ms, prof = timed(args.steps, True)
-    h.set_profiling(False)
+    total_ms = max(each(lambda r: r.timed(args.steps, False)[0]))
+    profs = each(lambda r: r.timed(args.steps, True))
+    prof_ms, prof = profs[0]
     clk = clocks.stop()
     if dist:
         dist.barrier()
-    value, max_ms = reduce_timing(total_ms, args.batch, args.steps, dist, dev)
+    n_units = len(runners)
+    value, max_ms = reduce_timing(total_ms, args.batch * n_units, args.steps, dist, runners[0].dev)
+    for r in runners:
+        r.check_outputs()
 
-    # parity spot check of this run's output rows (no oracle: finite values only)
-    out = d_out.cpu().numpy()
-    if not np.all(np.isfinite(out)):
-        raise RuntimeError("non-finite outputs in the timed run")
-
-    # e2e through the C ABI host path: pinned inputs -> H2D -> forward -> D2H rows, every step
-    h.spatial[:args.batch] = spatial
-    h.glob[:args.batch] = glob
-    for _ in range(max(3, args.warmup)):
-        h.enqueue(args.batch)
-        h.wait()
     if dist:
         dist.barrier()
-    e_s = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
-    e_e = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
-    for i in range(args.steps):
-        with torch.cuda.stream(stream):
-            flush.zero_()
-            e_s[i].record(stream)
-        h.enqueue(args.batch)
-        e_e[i].record(stream)
-        h.wait()
-    torch.cuda.synchronize()
-    e2e_ms = sum(e_s[i].elapsed_time(e_e[i]) for i in range(args.steps))
-    e2e_value, _ = reduce_timing(e2e_ms, args.batch, args.steps, dist, dev)
+    e2e_ms = max(each(lambda r: r.timed_e2e(args.steps)))
+    e2e_value, e2e_max_ms = reduce_timing(e2e_ms, args.batch * n_units, args.steps, dist, runners[0].dev)
 
     if rank == 0:
         burst, sustained, hbm, src = peaks()
@@ -365,41 +455,51 @@ def run_ours(args):
         if conv_n:
             flops_per_launch = conv3_row * args.batch * args.steps / conv_n
             achieved = flops_per_launch / (conv_ms / conv_n / 1e3) / 1e12
-            frac = achieved / sustained
+            frac = achieved / burst
         other = {k: {"ms_per_step": v[0] / args.steps, "launches_per_step": v[1] / args.steps}
                  for k, v in prof.items()}
+        h = runners[0].h
+        sizes = args.boards.replace(",", "/")
         line = {
-            "metric": metric_name(args), "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
-            "warmup": args.warmup, "ms_per_step": max_ms / args.steps, "higher_is_better": True, "scaling": "weak",
-            "vs_baseline": None, "dtype": args.precision, "data": "synthetic",
-            "config": {"workload": f"{args.net} forward pass, batch {args.batch} per GPU, {args.precision} "
-                                   "activations/f32 accumulation, seeded random-init weights",
-                       "net": args.net, "batch_per_gpu": args.batch,
-                       "parallelism": f"replicas x{world} (no collective)",
-                       "l2": "flushed between timed steps (256 MiB write, outside the timed events)"},
-            "roofline": {"bound": "tensor", "achieved": achieved, "peak": sustained, "unit": "TFLOP/s", "frac": frac,
-                         "traffic": CONV3_DRAM_BYTES_PER_LAUNCH if args.net == "b18c384nbt" and args.batch == 256
-                         else None,
+            "metric": metric_name(args), "value": value, "unit": UNIT, "n_gpus": world * n_units,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": max_ms / args.steps,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": args.precision,
+            "data": "synthetic",
+            "config": {"workload": f"{args.net} forward pass, batch {args.batch} per GPU of {sizes} boards, "
+                                   f"{args.precision} activations/f32 accumulation, seeded random-init weights "
+                                   "(He-normal / 1/sqrt(fan_in), last layer of each residual branch scaled by "
+                                   "1/sqrt(residual adds))",
+                       "net": args.net, "batch_per_gpu": args.batch, "boards": sizes,
+                       "parallelism": (f"{n_units} handles in one process, one host thread per GPU"
+                                       if in_process else f"replicas x{world} (one process per GPU)")
+                                      + ", no collective",
+                       "l2": "flushed between timed steps (256 MiB write, outside the timed region)"},
+            "roofline": {"bound": "tensor", "achieved": achieved, "peak": burst, "unit": "TFLOP/s", "frac": frac,
+                         "traffic": conv3_traffic(args),
                          "kernel": "gemm_pair_kernel (3x3 conv: CTA-pair tcgen05 implicit GEMM, windowed A)",
-                         "peak_kind": f"{src} bf16 sustained"},
+                         "peak_kind": f"{src} bf16 burst (the kernel is timed by its own launch events)"},
             "kernels": other,
             "profiled_ms_per_step": prof_ms / args.steps,
             "flops_per_eval": flops_row,
             "model_tflops": flops_row * value / 1e12,
             "e2e": {"value": e2e_value, "unit": UNIT,
                     "h2d_bytes_per_step": args.batch * (h.n_spatial + h.n_global) * 4,
-                    "d2h_bytes_per_step": args.batch * h.row_len * 4 + 4},
+                    "d2h_bytes_per_step": args.batch * h.row_len * 4 + 4,
+                    "ms_per_step": e2e_max_ms / args.steps,
+                    "timing": "host clock around kc_enqueue + kc_wait"},
             "gpu_launches": launches_per_step * args.steps,
             "clocks": clk,
         }
-        if world == 1 and not args.no_cpu_baseline:
+        if world == 1 and n_units == 1 and not args.no_cpu_baseline:
             v, n, el = cpu_baseline(args, args.cpu_seconds, threads=host_threads())
             line["cpu_baseline"] = {"value": v, "unit": UNIT, "cores": host_threads(), "kind": "port",
                                     "sample": f"{n} boards of the batch-{args.batch} workload in {el:.1f} s, "
-                                              "CPU oracle float32 (reference arithmetic restated in C++), "
+                                              "CPU oracle float32 (reference arithmetic restated in C++, an "
+                                              "unoptimised restatement, not the reference's flex backend), "
                                               "OpenMP on all host threads"}
         print(json.dumps(line), flush=True)
-    h.close()
+    for r in runners:
+        r.h.close()
     if dist:
         dist.destroy_process_group()
 

@@ -169,13 +169,23 @@ int kc_gpool_fc(const float* d_x, const float* d_mask, int n, int c, const float
  * KC_GPOOL_NOALLOC_MAX_FLOATS floats (1 MiB) in device memory, present on every GPU that loads this library until
  * the process exits; larger n * 3c is rejected with KC_ERR_INVALID. The first call on a device looks up that
  * array's device address (once per device, with that device current), so make the first call on each device
- * before any stream capture. All calls share the one array and it keeps the last call's contents (every entry a
+ * before any stream capture. With CUDA's lazy module loading (the default) the array is only placed in device
+ * memory when that first call loads this part of the library on the device: make the first call before reserving
+ * the device's memory for other pools (or load modules eagerly, CUDA_MODULE_LOADING=EAGER). All calls share the one array and it keeps the last call's contents (every entry a
  * call reads is written by that call first): calls whose work overlaps on the GPU (different streams, or
  * different host threads on one device) race on it and must be ordered by the caller. Inputs, outputs and
  * stream are as for kc_gpool_fc. */
 #define KC_GPOOL_NOALLOC_MAX_FLOATS 262144
 int kc_gpool_fc_noalloc(const float* d_x, const float* d_mask, int n, int c, const float* d_w, int oc, float* d_out,
                         void* stream);
+
+/* Failure-detection self-test. Every spin-wait in this library's kernels is bounded: when a wait runs out, the
+ * kernel records an error code in the handle's device error word, releases what it holds and returns, and the next
+ * kc_wait / kc_synchronize reports KC_ERR_DEVICE (the handle stays usable). This enqueues on the handle's stream
+ * one kernel that makes the same bounded wait on a barrier nothing completes, with a limit of `limit_us`
+ * microseconds (1 .. 2,000,000) instead of the forward pass's 2 s, so that a caller can check the whole error path
+ * without a fault. No counterpart in the reference, whose kernels have no bounded waits. */
+int kc_selftest_device_timeout(kc_handle* h, int limit_us);
 
 /* Host-side symmetry helpers of the reference (nninputs.rs:756-879), exported for tests of the host logic.
  * NCHW copy of one row with `c_size` channels; `reverse` = copyOutputsWithSymmetry semantics. */

@@ -7,11 +7,12 @@
 // fields by model version (:622-731).
 
 #include <chrono>
+#include <condition_variable>
 #include <cstdlib>
 #include <cstring>
 #include <memory>
+#include <mutex>
 #include <string>
-#include <thread>
 #include <vector>
 
 #include "common.h"
@@ -56,6 +57,10 @@ struct kc_handle {
   int last_n = 0;
   bool pending = false;
   std::vector<float> scratch;  // get_output: one row's symmetric copy
+  // completion: a host function enqueued behind each batch counts it done and wakes the waiter (no polling)
+  std::mutex mu;
+  std::condition_variable cv;
+  uint64_t enq_seq = 0, done_seq = 0;
 
   ~kc_handle() {
     if (stream) {
@@ -150,18 +155,43 @@ void check_device(int dev) {
                                ") is not an sm_100 (Blackwell B200) GPU");
 }
 
-void wait_event(kc_handle* h, int timeout_ms) {
-  auto t0 = std::chrono::steady_clock::now();
-  while (true) {
-    cudaError_t e = cudaEventQuery(h->done);
-    if (e == cudaSuccess) break;
-    if (e != cudaErrorNotReady) KC_CUDA(e);
-    if (timeout_ms >= 0 &&
-        std::chrono::duration_cast<std::chrono::milliseconds>(std::chrono::steady_clock::now() - t0).count() >
-            timeout_ms)
-      fail(KC_ERR_TIMEOUT, "CUDA backend: batch did not finish within " + std::to_string(timeout_ms) + " ms");
-    std::this_thread::sleep_for(std::chrono::microseconds(20));
+void CUDART_CB on_batch_done(void* arg) {
+  kc_handle* h = static_cast<kc_handle*>(arg);
+  {
+    std::lock_guard<std::mutex> lock(h->mu);
+    h->done_seq++;
   }
+  h->cv.notify_all();
+}
+
+// Record completion of everything enqueued so far on the handle's stream: an event (for error queries) and a host
+// function that wakes wait_event.
+void mark_batch(kc_handle* h) {
+  KC_CUDA(cudaEventRecord(h->done, h->stream));
+  {
+    std::lock_guard<std::mutex> lock(h->mu);
+    h->enq_seq++;
+  }
+  KC_CUDA(cudaLaunchHostFunc(h->stream, on_batch_done, h));
+  h->pending = true;
+}
+
+void wait_event(kc_handle* h, int timeout_ms) {
+  bool finished;
+  {
+    std::unique_lock<std::mutex> lock(h->mu);
+    auto done = [&] { return h->done_seq >= h->enq_seq; };
+    if (timeout_ms < 0) {
+      h->cv.wait(lock, done);
+      finished = true;
+    } else {
+      finished = h->cv.wait_for(lock, std::chrono::milliseconds(timeout_ms), done);
+    }
+  }
+  cudaError_t e = cudaEventQuery(h->done);
+  if (e != cudaSuccess && e != cudaErrorNotReady) KC_CUDA(e);
+  if (!finished)
+    fail(KC_ERR_TIMEOUT, "CUDA backend: batch did not finish within " + std::to_string(timeout_ms) + " ms");
   h->pending = false;
   if (*h->h_err != 0) {
     int code = *h->h_err;
@@ -188,9 +218,8 @@ void enqueue_host(kc_handle* h, int n) {
   const int row_len = h->engine->layout().row_len;
   KC_CUDA(cudaMemcpyAsync(h->h_out, h->d_out, (size_t)n * row_len * sizeof(float), cudaMemcpyDeviceToHost, h->stream));
   KC_CUDA(cudaMemcpyAsync(h->h_err, h->engine->error_word(), sizeof(int), cudaMemcpyDeviceToHost, h->stream));
-  KC_CUDA(cudaEventRecord(h->done, h->stream));
+  mark_batch(h);
   h->last_n = n;
-  h->pending = true;
 }
 
 }  // namespace
@@ -410,11 +439,11 @@ int kc_enqueue_device(kc_handle* h, int n, const float* d_spatial, const float* 
     need(d_global, "global");
     need(d_out, "out");
     if (h->n_meta) need(d_meta, "meta");
+    if (h->pending) fail(KC_ERR_INVALID, "CUDA backend: kc_enqueue_device while the previous batch was not waited for");
     KC_CUDA(cudaSetDevice(h->device));
     h->engine->forward(n, h->stream, d_spatial, d_global, h->n_meta ? d_meta : nullptr, d_out);
     KC_CUDA(cudaMemcpyAsync(h->h_err, h->engine->error_word(), sizeof(int), cudaMemcpyDeviceToHost, h->stream));
-    KC_CUDA(cudaEventRecord(h->done, h->stream));
-    h->pending = true;
+    mark_batch(h);
     h->last_n = n;
   });
 }
@@ -431,8 +460,7 @@ int kc_synchronize(kc_handle* h, int timeout_ms) {
   return guard([&] {
     need(h, "handle");
     KC_CUDA(cudaSetDevice(h->device));
-    KC_CUDA(cudaEventRecord(h->done, h->stream));
-    h->pending = true;
+    mark_batch(h);
     wait_event(h, timeout_ms);
   });
 }
@@ -450,6 +478,8 @@ int kc_get_output(kc_handle* h, int n, const float* const* spatial_rows, const f
     need(value_out, "value out");
     need(misc_out, "misc out");
     if (n < 1 || n > h->max_batch) fail(KC_ERR_INVALID, "CUDA backend: batch size out of range");
+    // the staging buffers below are still read by an earlier batch's copies while it is in flight
+    if (h->pending) fail(KC_ERR_INVALID, "CUDA backend: kc_get_output while an enqueued batch was not waited for");
     const kc::ModelDesc& m = h->model->desc;
     const int hw = 361;
     // copy_inputs (backend.rs:497-546): symmetry and optimism are read here, before the batch runs
@@ -531,6 +561,21 @@ int kc_handle_launch_count(kc_handle* h, int n, int* launches) {
     need(launches, "launches");
     (void)n;
     *launches = h->engine->launches_per_forward();
+  });
+}
+
+int kc_selftest_device_timeout(kc_handle* h, int limit_us) {
+  return guard([&] {
+    need(h, "handle");
+    if (limit_us < 1 || limit_us > 2000000) fail(KC_ERR_INVALID, "CUDA backend: self-test limit outside [1 us, 2 s]");
+    if (h->pending) fail(KC_ERR_INVALID, "CUDA backend: self-test while an enqueued batch was not waited for");
+    KC_CUDA(cudaSetDevice(h->device));
+    int khz = 0;
+    KC_CUDA(cudaDeviceGetAttribute(&khz, cudaDevAttrClockRate, h->device));
+    const long long cycles = (long long)limit_us * (khz > 0 ? khz : 2000000) / 1000;
+    kc::launch_wait_selftest(h->engine->error_word(), cycles, h->stream);
+    KC_CUDA(cudaMemcpyAsync(h->h_err, h->engine->error_word(), sizeof(int), cudaMemcpyDeviceToHost, h->stream));
+    mark_batch(h);
   });
 }
 

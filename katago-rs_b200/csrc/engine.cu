@@ -33,15 +33,16 @@ typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t,
                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
 
+// The driver's tensor-map encoder, looked up once per process (a function-local static: its initialisation is
+// thread-safe, and handles are built from several host threads at once when one process serves several GPUs).
 EncodeTiledFn encode_fn() {
-  static EncodeTiledFn fn = nullptr;
-  if (!fn) {
+  static const EncodeTiledFn fn = [] {
     void* p = nullptr;
     cudaDriverEntryPointQueryResult q;
     KC_CUDA(cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q));
     if (!p || q != cudaDriverEntryPointSuccess) fail(KC_ERR_CUDA, "CUDA backend: cuTensorMapEncodeTiled unavailable");
-    fn = reinterpret_cast<EncodeTiledFn>(p);
-  }
+    return reinterpret_cast<EncodeTiledFn>(p);
+  }();
   return fn;
 }
 
@@ -125,48 +126,46 @@ void launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cu
   KC_CUDA(cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...));
 }
 
-template <typename T, int BN, bool RF32, bool WIN>
+template <typename T, int BN, bool RF32>
 void launch_tc_bn(bool prepare, int grid, cudaStream_t s, const CUtensorMap& a, const CUtensorMap& b,
                   const GemmParams& p) {
-  using C = TcCfg<BN, WIN>;
+  using C = TcCfg<BN>;
   if (prepare) {
-    allow_smem(gemm_tc_kernel<T, BN, RF32, WIN>, C::SMEM);
+    allow_smem(gemm_tc_kernel<T, BN, RF32>, C::SMEM);
     return;
   }
-  launch_pdl(gemm_tc_kernel<T, BN, RF32, WIN>, dim3(grid), dim3(C::THREADS), C::SMEM, s, a, b, p);
+  launch_pdl(gemm_tc_kernel<T, BN, RF32>, dim3(grid), dim3(C::THREADS), C::SMEM, s, a, b, p);
 }
 
-template <typename T, bool RF32, bool WIN>
+template <typename T, bool RF32>
 void launch_tc_rf(bool prepare, int bn, int grid, cudaStream_t s, const CUtensorMap& a, const CUtensorMap& b,
                   const GemmParams& p) {
   switch (bn) {
-    case 16: launch_tc_bn<T, 16, RF32, WIN>(prepare, grid, s, a, b, p); break;
-    case 32: launch_tc_bn<T, 32, RF32, WIN>(prepare, grid, s, a, b, p); break;
-    case 48: launch_tc_bn<T, 48, RF32, WIN>(prepare, grid, s, a, b, p); break;
-    case 64: launch_tc_bn<T, 64, RF32, WIN>(prepare, grid, s, a, b, p); break;
-    case 96: launch_tc_bn<T, 96, RF32, WIN>(prepare, grid, s, a, b, p); break;
-    case 128: launch_tc_bn<T, 128, RF32, WIN>(prepare, grid, s, a, b, p); break;
-    case 192: launch_tc_bn<T, 192, RF32, WIN>(prepare, grid, s, a, b, p); break;
-    case 256: launch_tc_bn<T, 256, RF32, WIN>(prepare, grid, s, a, b, p); break;
+    case 16: launch_tc_bn<T, 16, RF32>(prepare, grid, s, a, b, p); break;
+    case 32: launch_tc_bn<T, 32, RF32>(prepare, grid, s, a, b, p); break;
+    case 48: launch_tc_bn<T, 48, RF32>(prepare, grid, s, a, b, p); break;
+    case 64: launch_tc_bn<T, 64, RF32>(prepare, grid, s, a, b, p); break;
+    case 96: launch_tc_bn<T, 96, RF32>(prepare, grid, s, a, b, p); break;
+    case 128: launch_tc_bn<T, 128, RF32>(prepare, grid, s, a, b, p); break;
+    case 192: launch_tc_bn<T, 192, RF32>(prepare, grid, s, a, b, p); break;
+    case 256: launch_tc_bn<T, 256, RF32>(prepare, grid, s, a, b, p); break;
     default: fail(KC_ERR_INVALID, "CUDA backend: unsupported GEMM tile width " + std::to_string(bn));
   }
 }
 
-// rf32: the GEMM's residual is a float32 stream (only the bf16 tier has those); win: windowed multi-tap A loads
+// rf32: the GEMM's residual is a float32 stream (only the bf16 tier has those)
 template <typename T>
-void launch_tc(bool prepare, bool rf32, bool win, int bn, int grid, cudaStream_t s, const CUtensorMap& a,
-               const CUtensorMap& b, const GemmParams& p) {
+void launch_tc(bool prepare, bool rf32, int bn, int grid, cudaStream_t s, const CUtensorMap& a, const CUtensorMap& b,
+               const GemmParams& p) {
   if constexpr (std::is_same<T, __nv_bfloat16>::value) {
     if (rf32) {
-      if (win) launch_tc_rf<T, true, true>(prepare, bn, grid, s, a, b, p);
-      else launch_tc_rf<T, true, false>(prepare, bn, grid, s, a, b, p);
+      launch_tc_rf<T, true>(prepare, bn, grid, s, a, b, p);
       return;
     }
   } else {
     if (rf32) fail(KC_ERR_INVALID, "CUDA backend: float32 residual stream outside the bf16 tier");
   }
-  if (win) launch_tc_rf<T, false, true>(prepare, bn, grid, s, a, b, p);
-  else launch_tc_rf<T, false, false>(prepare, bn, grid, s, a, b, p);
+  launch_tc_rf<T, false>(prepare, bn, grid, s, a, b, p);
 }
 
 // The CTA-pair GEMM, launched as clusters of two CTAs. `prepare` (plan-build time) opts the instance into its
@@ -234,14 +233,6 @@ int launch_pair(bool prepare, int bn, int kind, int pairs, cudaStream_t s, const
       fail(KC_ERR_INVALID, "CUDA backend: unsupported pair tile (" + std::to_string(kind) + ", " + std::to_string(bn) + ")");
   }
   return 0;
-}
-
-// How a windowed A start that is not a multiple of 8 rows is described to tcgen05. Measured on B200: the 128 B
-// swizzle follows the absolute shared-memory address bits, so the descriptor's base offset stays 0 (mode 1); the
-// row-phase base offset (mode 0) reads the wrong elements. KATAGO_CUDA_WIN_BASE overrides.
-int win_base_mode() {
-  const char* e = std::getenv("KATAGO_CUDA_WIN_BASE");
-  return e ? std::atoi(e) : 1;
 }
 
 // RoPE tables [tables][361][half] (desc.cpp computeRopeCosSin as restated in bin2onnx.py:449-484: float32 steps,
@@ -324,7 +315,13 @@ struct Engine::Impl {
   float* scale1 = nullptr;
   float* scale2 = nullptr;
   float* board_bias = nullptr;
-  std::map<std::tuple<int, const void*, const void*, const void*, void*>, cudaGraphExec_t> graphs;
+  // Captured forward passes by (batch size and profiling, caller's buffers), least recently used first out of
+  // `graph_lru` once more than kMaxGraphs are held (a caller that rotates buffers or batch sizes would otherwise
+  // keep one graph per combination). An evicted graph that is still running is freed when it completes.
+  using GraphKey = std::tuple<int, const void*, const void*, const void*, void*>;
+  static constexpr size_t kMaxGraphs = 64;
+  std::map<GraphKey, std::pair<cudaGraphExec_t, uint64_t>> graphs;
+  uint64_t graph_clock = 0;
 
   void* alloc(size_t bytes) {
     void* p = nullptr;
@@ -341,7 +338,7 @@ struct Engine::Impl {
     return p;
   }
   ~Impl() {
-    for (auto& g : graphs) cudaGraphExecDestroy(g.second);
+    for (auto& g : graphs) cudaGraphExecDestroy(g.second.first);
     for (void* p : allocs) cudaFree(p);
   }
 };
@@ -353,7 +350,7 @@ struct Engine::Impl {
 namespace {
 
 enum Role : int {
-  R_T1, R_REG, R_G, R_XN, R_QKV, R_O, R_H, R_AG, R_HEAD, R_P1A, R_STEM,
+  R_T1, R_REG, R_G, R_XN, R_QKV, R_O, R_H, R_AG, R_HEAD, R_P1A, R_STEM, R_TIPH,
   R_LEVEL0 = 16,  // + 2 * depth (+0 stream, +1 act)
   R_COUNT = 32
 };
@@ -361,6 +358,10 @@ enum FRole : int { F_POOL, F_GBIAS, F_VPOOL, F_V2, F_PASS, F_PIX, F_TIPSS, F_COU
 
 template <typename T>
 struct Builder {
+  // The heads' operand type: the bf16 tier runs the policy and value heads (under 0.3% of a transformer net's
+  // FLOPs) in f16, whose 11-bit significand keeps their rounding, the largest error term of the tier's outputs at
+  // bf16, well inside the tier's tolerance; the other tiers use their own type.
+  using H = typename std::conditional<std::is_same<T, __nv_bfloat16>::value, __half, T>::type;
   Engine::Impl& I;
   std::vector<Engine::Launch>& plan;
   const ModelDesc& m;
@@ -548,8 +549,11 @@ struct Builder {
     return 0;
   }
 
+  // E: the operand type of this GEMM (the tier's type, or __half for the heads of the bf16 tier)
+  template <typename E = T>
   void gemm(Spec s) {
     if (pass == 0) return;
+    constexpr bool ebf = std::is_same<E, __nv_bfloat16>::value;
     GemmParams p;
     p.n_total = s.N;
     p.cin = s.cin;
@@ -608,27 +612,14 @@ struct Builder {
     if (s.cin > s.A.ld) fail(KC_ERR_INVALID, "CUDA backend: GEMM reads more channels than its input holds");
     const int K = p.taps * s.cin;
     Engine::Impl* Ip = &I;
-    if constexpr (sizeof(T) == 2) {
+    if constexpr (sizeof(E) == 2) {
       // SwiGLU splits each tile's linear1 half between two epilogue warps (BN % 64); RoPE gives each warp whole
       // heads (BN % (2 * head_dim))
       int bn = pick_bn(s.N, s.mode == MODE_SWIGLU ? 64 : s.mode == MODE_ROPE ? 2 * s.head_dim : 16);
       if (!bn) fail(KC_ERR_INVALID, "CUDA backend: no GEMM tile width for N = " + std::to_string(s.N));
-      // KATAGO_CUDA_WIN=1: multi-tap convolutions load one A window per 64-channel chunk (the tile plus its tap
-      // halo) shared by all taps. Off by default: it cuts L2 traffic by a third, but the misaligned window starts
-      // cost shared-memory bandwidth the M = 128 MMA already needs (3x3 192->192 at batch 256: 94 us vs 88 us).
-      const char* wenv = std::getenv("KATAGO_CUDA_WIN");
-      bool win = p.taps > 1 && wenv && wenv[0] == '1';
-      if (win) {
-        int halo = 0;
-        for (int i = 0; i < p.taps; i++) halo = std::max(halo, std::abs(p.tap_off[i]));
-        p.halo = halo;
-        p.win_rows = round_up(128 + 2 * halo, 8);
-        p.win_base_mode = win_base_mode();
-        if (p.win_rows > TcCfg<256, true>::WIN_MAX_ROWS) win = false;
-      }
       if (s.cin % 64 != 0) fail(KC_ERR_INVALID, "CUDA backend: GEMM input channels not padded");
       bool pf32 = false;
-      const int pbn = win ? 0 : pair_tile(s, p, pf32);
+      const int pbn = pair_tile(s, p, pf32);
       // SwiGLU tiles: the weight columns in tiles of the kernel's width
       const int tbn = pbn ? pbn : bn;
       std::vector<float> Wp = s.W;
@@ -641,9 +632,9 @@ struct Builder {
             std::memcpy(&Wp[(size_t)(t * tbn + hb + j) * K], &s.W[(size_t)(F + t * hb + j) * K], K * sizeof(float));
           }
       }
-      std::vector<T> Wt(Wp.size());
-      for (size_t i = 0; i < Wp.size(); i++) Wt[i] = T(Wp[i]);
-      T* dW = up(Wt);
+      std::vector<E> Wt(Wp.size());
+      for (size_t i = 0; i < Wp.size(); i++) Wt[i] = E(Wp[i]);
+      E* dW = up(Wt);
       if (pbn) {
         // CTA-pair kernel with TMA-staged epilogue boxes (the trunk's convolutions, the token linears); the raw,
         // act and residual boxes each come from the (single) segment that has them
@@ -658,7 +649,7 @@ struct Builder {
           if (p.seg[i].flags & EPI_RESIDUAL) res = &g.res, p.pair_res_x = g.res_c0 - n0;
         }
         const Tensor& out0 = raw ? *raw : *act;
-        auto box = [&](const Tensor* t) { return make_box_map(t ? t->p : out0.p, bf16, t ? t->ld : out0.ld,
+        auto box = [&](const Tensor* t) { return make_box_map(t ? t->p : out0.p, ebf, t ? t->ld : out0.ld,
                                                               rows_for(t ? *t : out0), t && t->f32); };
         // 3x3 convolutions read one A window per 64-channel chunk (KATAGO_CUDA_PAIR_WIN=0: one A tile per tap)
         const char* pw = std::getenv("KATAGO_CUDA_PAIR_WIN");
@@ -671,8 +662,8 @@ struct Builder {
           if (p.win_rows > PairCfg<256, true>::WIN_MAX_ROWS) pwin = false;
         }
         PairMaps pm;
-        pm.a = make_map(s.A.p, bf16, s.A.ld, a_rows, pwin ? p.win_rows : 128);
-        pm.b = make_map(dW, bf16, K, s.N, pbn / 2);
+        pm.a = make_map(s.A.p, ebf, s.A.ld, a_rows, pwin ? p.win_rows : 128);
+        pm.b = make_map(dW, ebf, K, s.N, pbn / 2);
         pm.res = box(res);
         pm.raw = box(raw);
         pm.act = box(act);
@@ -683,7 +674,7 @@ struct Builder {
           p.rope_sin = s.rope_sin_rows;
           p.rope_table_stride = s.rope_table_stride ? 432 * (s.head_dim / 2) : 0;
         }
-        const int max_pairs = launch_pair<T>(true, pbn, kind, 0, 0, pm, p);
+        const int max_pairs = launch_pair<E>(true, pbn, kind, 0, 0, pm, p);
         // Small batches: the convolutions also get 64-column tiles (three or six per row tile instead of one or two)
         // when that spreads a launch over more SM pairs than it adds tile rounds (KATAGO_CUDA_PAIR_NARROW=0: off).
         // A tile costs about its width plus a fixed ~74 columns' worth (prologue, pipeline fill, epilogue).
@@ -692,8 +683,8 @@ struct Builder {
         PairMaps pm64 = pm;
         int max_pairs64 = 0;
         if (narrow) {
-          pm64.b = make_map(dW, bf16, K, s.N, 32);
-          max_pairs64 = launch_pair<T>(true, 64, kind, 0, 0, pm64, p);
+          pm64.b = make_map(dW, ebf, K, s.N, 32);
+          max_pairs64 = launch_pair<E>(true, 64, kind, 0, 0, pm64, p);
         }
         add(s.cls, [=](cudaStream_t st, int n) {
           GemmParams q = p;
@@ -705,25 +696,25 @@ struct Builder {
             const long long cost = (long long)((tiles + max_pairs - 1) / max_pairs) * (pbn + 74);
             const long long cost64 = (long long)((tiles64 + max_pairs64 - 1) / max_pairs64) * (64 + 74);
             if (cost64 < cost) {
-              launch_pair<T>(false, 64, kind, std::min(tiles64, max_pairs64), st, pm64, q);
+              launch_pair<E>(false, 64, kind, std::min(tiles64, max_pairs64), st, pm64, q);
               return;
             }
           }
-          launch_pair<T>(false, pbn, kind, std::min(tiles, max_pairs), st, pm, q);
+          launch_pair<E>(false, pbn, kind, std::min(tiles, max_pairs), st, pm, q);
         });
         return;
       }
-      CUtensorMap ta = make_map(s.A.p, bf16, s.A.ld, a_rows, win ? p.win_rows : 128);
-      CUtensorMap tb = make_map(dW, bf16, K, s.N, bn);
+      CUtensorMap ta = make_map(s.A.p, ebf, s.A.ld, a_rows, 128);
+      CUtensorMap tb = make_map(dW, ebf, K, s.N, bn);
       bool rf32 = false;
       for (int i = 0; i < p.nseg; i++) rf32 = rf32 || (p.seg[i].flags & EPI_RES_F32);
-      launch_tc<T>(true, rf32, win, bn, 0, 0, ta, tb, p);
+      launch_tc<E>(true, rf32, bn, 0, 0, ta, tb, p);
       add(s.cls, [=](cudaStream_t st, int n) {
         GemmParams q = p;
         q.g.rows = n * brows;
         int tiles = ((q.g.rows + 127) / 128) * (q.n_total / bn);
         int grid = std::min(tiles, Ip->sm_count);
-        launch_tc<T>(false, rf32, win, bn, grid, st, ta, tb, q);
+        launch_tc<E>(false, rf32, bn, grid, st, ta, tb, q);
       });
     } else {
       p.a = s.A.p;
@@ -737,7 +728,7 @@ struct Builder {
         GemmParams q = p;
         q.g.rows = n * brows;
         dim3 grid((q.g.rows + 63) / 64, (q.n_total + 63) / 64);
-        launch_pdl(gemm_simt_kernel<T>, dim3(grid), dim3(SIMT_THREADS), 0, st, q);
+        launch_pdl(gemm_simt_kernel<E>, dim3(grid), dim3(SIMT_THREADS), 0, st, q);
       });
     }
   }
@@ -813,6 +804,7 @@ struct Builder {
   }
 
   // ---- elementwise / reduction launches ----
+  template <typename TI = T, typename TO = T>
   void bias_bnact(Tensor x, int xc0, const float* board_bias, const BNDesc& bn, Act act, int C, Tensor y) {
     const float* sc = up(bn.merged_scale);
     const float* bi = up(bn.merged_bias);
@@ -826,17 +818,18 @@ struct Builder {
       const int rows = n * 400;
       const unsigned blocks = (unsigned)(((size_t)rows * (Cw / 8) + 255) / 256);
       auto go = [&](auto kernel) {
-        launch_pdl(kernel, dim3(blocks), dim3(256), 0, st, (const T*)x.p, x.ld, xc0, board_bias, sc, bi, Ip->rowmask, rows, C, Cw,
-                                       (T*)y.p, y.ld);
+        launch_pdl(kernel, dim3(blocks), dim3(256), 0, st, (const TI*)x.p, x.ld, xc0, board_bias, sc, bi, Ip->rowmask,
+                   rows, C, Cw, (TO*)y.p, y.ld);
       };
       switch (act) {
-        case 1: go(bias_bnact_kernel<T, 1>); break;
-        case 2: go(bias_bnact_kernel<T, 2>); break;
-        case 3: go(bias_bnact_kernel<T, 3>); break;
-        default: go(bias_bnact_kernel<T, 0>); break;
+        case 1: go(bias_bnact_kernel<TI, TO, 1>); break;
+        case 2: go(bias_bnact_kernel<TI, TO, 2>); break;
+        case 3: go(bias_bnact_kernel<TI, TO, 3>); break;
+        default: go(bias_bnact_kernel<TI, TO, 0>); break;
       }
     });
   }
+  template <typename E = T>
   void pool(Tensor x, int c0, int C, bool value_mode, float* out) {
     Engine::Impl* Ip = &I;
     const int CG = (C + 7) / 8;
@@ -844,7 +837,7 @@ struct Builder {
       fail(KC_ERR_INVALID, "CUDA backend: pooled channels unaligned or too many");
     const int smem = 2 * (POOL_THREADS / CG) * CG * 8 * (int)sizeof(float);
     add(CLS_OTHER, [=](cudaStream_t st, int n) {
-      launch_pdl(pool_kernel<T>, dim3(n), dim3(POOL_THREADS), smem, st, (const T*)x.p, x.ld, c0, C, Ip->rowmask, Ip->mask_sum,
+      launch_pdl(pool_kernel<E>, dim3(n), dim3(POOL_THREADS), smem, st, (const E*)x.p, x.ld, c0, C, Ip->rowmask, Ip->mask_sum,
                                                     Ip->scale1, Ip->scale2, value_mode ? 1 : 0, out);
     });
   }
@@ -1277,10 +1270,16 @@ struct Builder {
       s.segs = {g};
       gemm(std::move(s));
     }
-    // trunk
+    // trunk; with heads in another type than the trunk (the bf16 tier) the tip writes its own buffer in that type
+    constexpr bool hsplit = !std::is_same<H, T>::value;
     BnAct tip;
-    if (m.trunk_norm_kind == 0) tip = {&m.tip_bn, m.tip_act};
+    if (m.trunk_norm_kind == 0 && !hsplit) tip = {&m.tip_bn, m.tip_act};
     emit_stack(m.blocks, 0, C, tip);
+    const Tensor XH = hsplit ? tensor(R_TIPH, C) : XA;
+    if (m.trunk_norm_kind == 0 && hsplit) {
+      if (X.f32) bias_bnact<float, H>(X, 0, nullptr, m.tip_bn, m.tip_act, C, XH);
+      else bias_bnact<T, H>(X, 0, nullptr, m.tip_bn, m.tip_act, C, XH);
+    }
     if (m.trunk_norm_kind != 0) {
       const float* g = up(m.tip_rms_gamma);
       const float* bb = up(m.tip_rms_beta);
@@ -1288,18 +1287,18 @@ struct Builder {
       int spatial = m.tip_rms_spatial ? 1 : 0;
       int act = m.tip_act;
       Engine::Impl* Ip = &I;
-      if (!spatial && rms_vec(X, C, XA)) {
+      if (!spatial && rms_vec(X, C, XH)) {
         // per-point tip: one warp per row
         add(CLS_OTHER, [=](cudaStream_t st, int n) {
           const int rows = n * 400;
           if (X.f32)
-            launch_pdl(rms_rows_kernel<float, T, true>, dim3((rows + 7) / 8), dim3(256), 0, st, (const float*)X.p,
-                       X.ld, C / 128, g, bb, act, eps, Ip->rowmask, rows, (T*)XA.p, XA.ld);
+            launch_pdl(rms_rows_kernel<float, H, true>, dim3((rows + 7) / 8), dim3(256), 0, st, (const float*)X.p,
+                       X.ld, C / 128, g, bb, act, eps, Ip->rowmask, rows, (H*)XH.p, XH.ld);
           else
-            launch_pdl(rms_rows_kernel<T, T, true>, dim3((rows + 7) / 8), dim3(256), 0, st, (const T*)X.p, X.ld,
-                       C / 128, g, bb, act, eps, Ip->rowmask, rows, (T*)XA.p, XA.ld);
+            launch_pdl(rms_rows_kernel<T, H, true>, dim3((rows + 7) / 8), dim3(256), 0, st, (const T*)X.p, X.ld,
+                       C / 128, g, bb, act, eps, Ip->rowmask, rows, (H*)XH.p, XH.ld);
         });
-      } else if (spatial && rms_vec(X, C, XA)) {
+      } else if (spatial && rms_vec(X, C, XH)) {
         // spatial tip: row sums of squares, then per row its board's rms and the affine + activation
         float* tss = fbuffer(F_TIPSS, 400);
         add(CLS_OTHER, [=](cudaStream_t st, int n) {
@@ -1307,22 +1306,22 @@ struct Builder {
           const dim3 grid((rows + 7) / 8), block(256);
           if (X.f32) {
             launch_pdl(row_sumsq_kernel<float>, grid, block, 0, st, (const float*)X.p, X.ld, C / 128, rows, tss);
-            launch_pdl(tip_spatial_apply_kernel<float, T>, grid, block, 0, st, (const float*)X.p, X.ld, C / 128,
-                       (const float*)tss, Ip->rowmask, Ip->mask_sum, g, bb, act, eps, rows, (T*)XA.p, XA.ld);
+            launch_pdl(tip_spatial_apply_kernel<float, H>, grid, block, 0, st, (const float*)X.p, X.ld, C / 128,
+                       (const float*)tss, Ip->rowmask, Ip->mask_sum, g, bb, act, eps, rows, (H*)XH.p, XH.ld);
           } else {
             launch_pdl(row_sumsq_kernel<T>, grid, block, 0, st, (const T*)X.p, X.ld, C / 128, rows, tss);
-            launch_pdl(tip_spatial_apply_kernel<T, T>, grid, block, 0, st, (const T*)X.p, X.ld, C / 128,
-                       (const float*)tss, Ip->rowmask, Ip->mask_sum, g, bb, act, eps, rows, (T*)XA.p, XA.ld);
+            launch_pdl(tip_spatial_apply_kernel<T, H>, grid, block, 0, st, (const T*)X.p, X.ld, C / 128,
+                       (const float*)tss, Ip->rowmask, Ip->mask_sum, g, bb, act, eps, rows, (H*)XH.p, XH.ld);
           }
         });
       } else {
         add(CLS_OTHER, [=](cudaStream_t st, int n) {
           if (X.f32)
-            launch_pdl(tip_rms_kernel<float, T>, dim3(n), dim3(512), 0, st, (const float*)X.p, X.ld, C, g, bb, eps, spatial, act,
-                                                        Ip->rowmask, Ip->mask_sum, (T*)XA.p, XA.ld);
+            launch_pdl(tip_rms_kernel<float, H>, dim3(n), dim3(512), 0, st, (const float*)X.p, X.ld, C, g, bb, eps,
+                       spatial, act, Ip->rowmask, Ip->mask_sum, (H*)XH.p, XH.ld);
           else
-            launch_pdl(tip_rms_kernel<T, T>, dim3(n), dim3(512), 0, st, (const T*)X.p, X.ld, C, g, bb, eps, spatial, act, Ip->rowmask,
-                                                    Ip->mask_sum, (T*)XA.p, XA.ld);
+            launch_pdl(tip_rms_kernel<T, H>, dim3(n), dim3(512), 0, st, (const T*)X.p, X.ld, C, g, bb, eps, spatial,
+                       act, Ip->rowmask, Ip->mask_sum, (H*)XH.p, XH.ld);
         });
       }
     }
@@ -1339,7 +1338,7 @@ struct Builder {
       // HEAD column = GEMM column: each segment's output base is its first GEMM column
       Seg s1 = act_seg(G1p, m.g1_bn, m.g1_act, HEAD, P1p);
       Seg s2 = act_seg(V1p, m.v1_bn, m.v1_act, HEAD, P1p + G1p);
-      gemm(conv_spec(CLS_LINEAR, XA, C, {&m.p1_conv, &m.g1_conv, &m.v1_conv}, {s0, s1, s2}));
+      gemm<H>(conv_spec(CLS_LINEAR, XH, C, {&m.p1_conv, &m.g1_conv, &m.v1_conv}, {s0, s1, s2}));
     }
     L.policy_off = 0;
     L.value_off = m.num_policy_channels * 362;
@@ -1349,9 +1348,9 @@ struct Builder {
     const int row_len = L.row_len;
     float* g1pool = fbuffer(F_POOL, 3 * g1c);
     float* p1bias = fbuffer(F_GBIAS, p1c);
-    pool(HEAD, P1p, g1c, false, g1pool);
+    pool<H>(HEAD, P1p, g1c, false, g1pool);
     fc(g1pool, 3 * g1c, m.gpool_to_bias_mul, nullptr, ACT_IDENTITY, p1bias, p1c, 0, 1);
-    bias_bnact(HEAD, 0, p1bias, m.p1_bn, m.p1_act, p1c, P1A);
+    bias_bnact<H, H>(HEAD, 0, p1bias, m.p1_bn, m.p1_act, p1c, P1A);
     {
       // p2 weights [p1c][P] and ownership weights [v1c] (1x1 convs, file order [ic][oc])
       const float* w2 = up(m.p2_conv.w);
@@ -1360,9 +1359,8 @@ struct Builder {
       const int v1c0 = P1p + G1p;
       Engine::Impl* Ip = &I;
       add(CLS_OTHER, [=](cudaStream_t st, int n) {
-        launch_pdl(head_spatial_kernel<T>, dim3((n * 361 + 127) / 128), dim3(128), 0, st, (const T*)P1A.p, P1A.ld, p1c, w2, P,
-                                                                     (const T*)HEAD.p, HEAD.ld, v1c0, v1c, wo, Ip->out,
-                                                                     row_len, own_off, n);
+        launch_pdl(head_spatial_kernel<H>, dim3((n * 361 + 127) / 128), dim3(128), 0, st, (const H*)P1A.p, P1A.ld,
+                   p1c, w2, P, (const H*)HEAD.p, HEAD.ld, v1c0, v1c, wo, Ip->out, row_len, own_off, n);
       });
     }
     // pass logit: policy[p * 362 + 361]
@@ -1376,7 +1374,7 @@ struct Builder {
     // value head
     float* vpool = fbuffer(F_VPOOL, 3 * v1c);
     float* v2 = fbuffer(F_V2, m.v2_mul.oc);
-    pool(HEAD, P1p + G1p, v1c, true, vpool);
+    pool<H>(HEAD, P1p + G1p, v1c, true, vpool);
     fc(vpool, 3 * v1c, m.v2_mul, &m.v2_bias, m.v2_act, v2, m.v2_mul.oc, 0, 1);
     fc(v2, m.v2_mul.oc, m.v3_mul, &m.v3_bias, ACT_IDENTITY, nullptr, row_len, L.value_off, 1);
     fc(v2, m.v2_mul.oc, m.sv3_mul, &m.sv3_bias, ACT_IDENTITY, nullptr, row_len, L.score_off, 1);
@@ -1519,9 +1517,17 @@ void Engine::forward(int n, cudaStream_t stream, const float* d_spatial, const f
       cudaGraphExec_t ge;
       KC_CUDA(cudaGraphInstantiate(&ge, g, 0));
       cudaGraphDestroy(g);
-      it = I.graphs.emplace(key, ge).first;
+      if (I.graphs.size() >= Impl::kMaxGraphs) {
+        auto lru = I.graphs.begin();
+        for (auto j = I.graphs.begin(); j != I.graphs.end(); ++j)
+          if (j->second.second < lru->second.second) lru = j;
+        cudaGraphExecDestroy(lru->second.first);
+        I.graphs.erase(lru);
+      }
+      it = I.graphs.emplace(key, std::make_pair(ge, uint64_t(0))).first;
     }
-    KC_CUDA(cudaGraphLaunch(it->second, stream));
+    it->second.second = ++I.graph_clock;
+    KC_CUDA(cudaGraphLaunch(it->second.first, stream));
   }
   if (events) prof_pending_ = true;
 }

@@ -73,6 +73,10 @@ class Engine {
   void collect_profile();
 };
 
+// Failure-detection self-test (ops.cu): enqueue on `st` one kernel whose bounded wait runs out after
+// `limit_cycles` SM cycles and records DEV_TIMEOUT_TEST in `err`.
+void launch_wait_selftest(int* err, long long limit_cycles, cudaStream_t st);
+
 // Algorithmic FLOPs per board (direct-convolution MACs x 2 over the 361 points, attention over 361 x 361).
 void model_flops(const ModelDesc& m, double* total, double* conv3x3);
 

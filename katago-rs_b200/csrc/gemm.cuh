@@ -90,9 +90,8 @@ struct alignas(16) GemmParams {
   int rope_table_stride = 0;        // floats between tables (0: one shared table)
   int rope_q_cols = 0, rope_rot_cols = 0, head_dim = 0, rope_group = 1;
   int* err = nullptr;
-  // windowed A (tensor-core kernel with WIN): one window of win_rows rows starting halo rows above the tile
+  // windowed A (CTA-pair kernel, 3x3 convolutions): one window of win_rows rows starting halo rows above the tile
   int halo = 0, win_rows = 0;
-  int win_base_mode = 1;  // descriptor base offset of a shifted window start: 0 = its 128 B row phase, 1 = zero
   // CTA-pair kernel: columns >= pair_split belong to segment 1; the x coordinate of an output / residual box is
   // pair_*_x + GEMM column (the segment's c0 minus its first column)
   int pair_split = 0, pair_raw_x = 0, pair_act_x = 0, pair_res_x = 0;
@@ -282,29 +281,24 @@ __device__ __forceinline__ void epi_apply(const EpiSeg& s, const RowInfo& ri, in
 // tcgen05 persistent kernel
 // ================================================================================================================
 
-// Shared-memory plan of the tensor-core kernel. Without WIN a stage holds one A tile (128 rows x 64 channels) and
-// one B tile; with WIN (multi-tap convolutions) a ring of two A windows (up to 256 rows x 64 channels: the tile plus
-// its tap halo, loaded once per 64-channel chunk and shared by all taps) sits in front of B-only stages.
-template <int BN, bool WIN = false>
+// Shared-memory plan of the tensor-core kernel: a stage holds one A tile (128 rows x 64 channels) and one B tile.
+template <int BN>
 struct TcCfg {
   static constexpr int A_BYTES = 128 * 64 * 2;
   static constexpr int B_BYTES = BN * 64 * 2;
-  static constexpr int WIN_MAX_ROWS = 256;
-  static constexpr int A_WIN_BYTES = WIN_MAX_ROWS * 128;
-  static constexpr int A_RING_BYTES = WIN ? 2 * A_WIN_BYTES : 0;
-  static constexpr int STAGE_BYTES = WIN ? B_BYTES : A_BYTES + B_BYTES;
+  static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
   static constexpr int PARAM_COLS = 768;  // per-column BN scale and bias staged in shared memory
   static constexpr int PARAM_BYTES = PARAM_COLS * 2 * 4;
   static constexpr int BAR_BYTES = 256;
   static constexpr int PCOPY_BYTES = 1024;  // a shared-memory copy of GemmParams
   static constexpr int SMEM_LIMIT = 227 * 1024;
   static constexpr int FIT =
-      (SMEM_LIMIT - 1024 - BAR_BYTES - PARAM_BYTES - PCOPY_BYTES - A_RING_BYTES) / STAGE_BYTES;
+      (SMEM_LIMIT - 1024 - BAR_BYTES - PARAM_BYTES - PCOPY_BYTES) / STAGE_BYTES;
   static constexpr int STAGES = FIT > 8 ? 8 : FIT;
   static constexpr uint32_t ACC_COLS = BN <= 32 ? 32 : BN <= 64 ? 64 : BN <= 128 ? 128 : 256;
   static constexpr uint32_t TMEM_COLS = 2 * ACC_COLS;
   static constexpr int SMEM =
-      1024 /*align slack*/ + A_RING_BYTES + STAGES * STAGE_BYTES + BAR_BYTES + PARAM_BYTES + PCOPY_BYTES;
+      1024 /*align slack*/ + STAGES * STAGE_BYTES + BAR_BYTES + PARAM_BYTES + PCOPY_BYTES;
   static constexpr int EPI_WARPS = 8;  // two per TMEM lane quarter, splitting the tile's columns
   static constexpr int THREADS = 64 + 32 * EPI_WARPS;
 };
@@ -500,26 +494,23 @@ __device__ __forceinline__ void tc_epilogue_tile(const GemmParams& p, const EpiS
 }
 
 // RF32: the residual segments read a float32 residual stream (the bf16 tier).
-// WIN: multi-tap convolution with one A window per 64-channel chunk shared by all taps (TcCfg).
-template <typename T, int BN, bool RF32, bool WIN>
-__global__ void __launch_bounds__(TcCfg<BN, WIN>::THREADS, 1)
+template <typename T, int BN, bool RF32>
+__global__ void __launch_bounds__(TcCfg<BN>::THREADS, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                    const __grid_constant__ GemmParams p) {
-  using C = TcCfg<BN, WIN>;
+  using C = TcCfg<BN>;
   constexpr int fmt = sizeof(T) == 2 && std::is_same<T, __nv_bfloat16>::value ? 1 : 0;
   constexpr uint32_t IDESC = make_idesc_f16(fmt, 128, BN);
 
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t* stages = smem + C::A_RING_BYTES;  // WIN: the two A windows come first
+  uint8_t* stages = smem;
   uint64_t* full = reinterpret_cast<uint64_t*>(stages + C::STAGES * C::STAGE_BYTES);
   uint64_t* empty = full + C::STAGES;
   uint64_t* tfull = empty + C::STAGES;
   uint64_t* tempty = tfull + 2;
   uint64_t* drain = tempty + 2;
-  uint64_t* afull = drain + 1;
-  uint64_t* aempty = afull + 2;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(aempty + 2);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   float* s_scale = reinterpret_cast<float*>(stages + C::STAGES * C::STAGE_BYTES + C::BAR_BYTES);
   float* s_bias = s_scale + C::PARAM_COLS;
@@ -557,8 +548,6 @@ __global__ void __launch_bounds__(TcCfg<BN, WIN>::THREADS, 1)
     for (int a = 0; a < 2; a++) {
       mbar_init(&tfull[a], 1);
       mbar_init(&tempty[a], 32 * C::EPI_WARPS);
-      mbar_init(&afull[a], 1);
-      mbar_init(&aempty[a], 1);
     }
     mbar_init(drain, 1);
     *abort_flag = 0;
@@ -584,40 +573,10 @@ __global__ void __launch_bounds__(TcCfg<BN, WIN>::THREADS, 1)
       int stage = 0;
       uint32_t phase = 0;
       bool ok = true;
-      int as = 0;
-      uint32_t aph = 0;
       for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
         const int m0 = (tile / n_tiles) * 128;
         const int n0 = (tile % n_tiles) * BN;
-        if constexpr (WIN) {
-          // per 64-channel chunk: one A window (rows m0 - halo ...), then the chunk's B tile of every tap
-          for (int ch = 0; ch < kb_per_tap && ok; ch++) {
-            if (!mbar_wait(&aempty[as], aph ^ 1, p.err, DEV_TIMEOUT_PRODUCER) || *abort_flag) {
-              ok = false;
-              *abort_flag = 1;
-              break;
-            }
-            mbar_expect_tx(&afull[as], (uint32_t)p.win_rows * 128u);
-            tma_load_2d(smem + as * C::A_WIN_BYTES, &tmA, &afull[as], ch * 64, m0 - p.halo);
-            if (++as == 2) {
-              as = 0;
-              aph ^= 1;
-            }
-            for (int tap = 0; tap < p.taps; tap++) {
-              if (!mbar_wait(&empty[stage], phase ^ 1, p.err, DEV_TIMEOUT_PRODUCER) || *abort_flag) {
-                ok = false;
-                *abort_flag = 1;
-                break;
-              }
-              mbar_expect_tx(&full[stage], C::B_BYTES);
-              tma_load_2d(stages + stage * C::STAGE_BYTES, &tmB, &full[stage], tap * p.cin + ch * 64, n0);
-              if (++stage == C::STAGES) {
-                stage = 0;
-                phase ^= 1;
-              }
-            }
-          }
-        } else {
+        {
           for (int kb = 0; kb < KB; kb++) {
             if (!mbar_wait(&empty[stage], phase ^ 1, p.err, DEV_TIMEOUT_PRODUCER) || *abort_flag) {
               ok = false;
@@ -650,8 +609,6 @@ __global__ void __launch_bounds__(TcCfg<BN, WIN>::THREADS, 1)
       // ---- MMA issuer ----
       int stage = 0;
       uint32_t phase = 0;
-      int as = 0;
-      uint32_t aph = 0;
       int local = 0;
       bool ok = true;
       for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x, local++) {
@@ -663,42 +620,7 @@ __global__ void __launch_bounds__(TcCfg<BN, WIN>::THREADS, 1)
         }
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + acc * C::ACC_COLS;
-        if constexpr (WIN) {
-          for (int ch = 0; ch < kb_per_tap && ok; ch++) {
-            if (!mbar_wait(&afull[as], aph, p.err, DEV_TIMEOUT_MMA) || *abort_flag) {
-              ok = false;
-              break;
-            }
-            const uint32_t swin = smem_u32(smem + as * C::A_WIN_BYTES);
-            for (int tap = 0; tap < p.taps; tap++) {
-              if (!mbar_wait(&full[stage], phase, p.err, DEV_TIMEOUT_MMA) || *abort_flag) {
-                ok = false;
-                break;
-              }
-              tc_fence_after();
-              // the tap's 128-row A tile starts halo + tap_off rows into the window
-              const int r0 = p.halo + s_params->tap_off[tap];
-              const uint32_t sa = swin + (uint32_t)r0 * 128u;
-              const uint32_t boff = p.win_base_mode == 0 ? (uint32_t)(r0 & 7) : 0u;
-              const uint32_t sb = smem_u32(stages + stage * C::STAGE_BYTES);
-#pragma unroll
-              for (int k = 0; k < 4; k++)
-                umma_f16(d_tmem, make_sw128_desc(sa + k * 32, boff), make_sw128_desc(sb + k * 32), IDESC,
-                         (ch | tap | k) != 0);
-              umma_commit(&empty[stage]);
-              if (++stage == C::STAGES) {
-                stage = 0;
-                phase ^= 1;
-              }
-            }
-            if (!ok) break;
-            umma_commit(&aempty[as]);
-            if (++as == 2) {
-              as = 0;
-              aph ^= 1;
-            }
-          }
-        } else {
+        {
           // Two K-blocks (8 MMAs) per barrier wait and commit: tcgen05.mma issue blocks once a few MMAs are
           // queued, so the wait / commit latency between groups would otherwise idle the tensor pipe; with 4 MMAs
           // per group it cost a third of the throughput, with 8 under 2%.

@@ -298,8 +298,8 @@ __global__ void __launch_bounds__(FC_THREADS) fc_kernel(const float* __restrict_
 // ---------------------------------------------------------------------------------------------------------------
 // One thread per 8 channels of a row (16-byte loads and stores); the activation fixed at compile time. x's and y's
 // row pitches and xc0 are multiples of 8 elements, Cw a multiple of 8.
-template <typename T, int ACT>
-__global__ void bias_bnact_kernel(const T* __restrict__ x, int xld, int xc0, const float* __restrict__ board_bias,
+template <typename TI, typename T, int ACT>
+__global__ void bias_bnact_kernel(const TI* __restrict__ x, int xld, int xc0, const float* __restrict__ board_bias,
                                   const float* __restrict__ scale, const float* __restrict__ bias,
                                   const float* __restrict__ rowmask, int rows, int C, int Cw, T* __restrict__ y,
                                   int yld) {
@@ -314,7 +314,7 @@ __global__ void bias_bnact_kernel(const T* __restrict__ x, int xld, int xc0, con
   float o[8];
   if (c < C && m != 0.0f) {
     float v[8];
-    load_vec<T, 8>(x + (size_t)r * xld + xc0 + c, v);
+    load_vec<TI, 8>(x + (size_t)r * xld + xc0 + c, v);
     const float* bb = board_bias ? board_bias + (size_t)(r / 400) * C : nullptr;
     if (c + 8 <= C && (C & 3) == 0) {
       // whole vector inside the channels: parameters as 16-byte loads

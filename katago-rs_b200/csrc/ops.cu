@@ -77,6 +77,25 @@ void launch_gpool_fc(const float* x, const float* mask, int n, int c, const floa
   KC_CUDA(cudaGetLastError());
 }
 
+// Failure-detection self-test: one thread waits on an mbarrier that nothing arrives at, with the bounded wait
+// every kernel of the forward pass uses but a short limit; when the limit runs out it records `code` in the error
+// word (first error wins) and the kernel returns.
+__global__ void wait_selftest_kernel(int* err, long long limit_cycles) {
+  __shared__ __align__(8) uint64_t bar;
+  if (threadIdx.x == 0) {
+    mbar_init(&bar, 1);
+    fence_mbar_init();
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) mbar_wait_limit(&bar, 0, err, DEV_TIMEOUT_TEST, limit_cycles);
+  __syncthreads();
+}
+
+void launch_wait_selftest(int* err, long long limit_cycles, cudaStream_t st) {
+  wait_selftest_kernel<<<1, 32, 0, st>>>(err, limit_cycles);
+  KC_CUDA(cudaGetLastError());
+}
+
 }  // namespace kc
 
 namespace {

@@ -48,17 +48,6 @@ __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
 
 __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   uint32_t ok;
-#ifdef KC_MBAR_TEST_WAIT
-  asm volatile(
-      "{\n"
-      " .reg .pred p;\n"
-      " mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n"
-      " selp.u32 %0, 1, 0, p;\n"
-      "}\n"
-      : "=r"(ok)
-      : "r"(smem_u32(bar)), "r"(parity)
-      : "memory");
-#else
   asm volatile(
       "{\n"
       " .reg .pred p;\n"
@@ -68,7 +57,6 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
       : "=r"(ok)
       : "r"(smem_u32(bar)), "r"(parity)
       : "memory");
-#endif
   return ok != 0;
 }
 
@@ -78,17 +66,21 @@ constexpr long long kWaitLimitCycles = 4000ll * 1000ll * 1000ll;
 // Wait for the phase with `parity` to complete; false (and the error word set) if it did not within the limit.
 // The limit is checked on the SM's own cycle counter, and only every 256 polls: reading the global timer on every
 // miss put microseconds of latency on each pipeline hand-off.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* err, int code) {
+__device__ __forceinline__ bool mbar_wait_limit(uint64_t* bar, uint32_t parity, int* err, int code,
+                                                long long limit_cycles) {
   if (mbar_try_wait(bar, parity)) return true;
   const long long t0 = clock64();
   while (true) {
     for (int i = 0; i < 256; i++)
       if (mbar_try_wait(bar, parity)) return true;
-    if (clock64() - t0 > kWaitLimitCycles) {
+    if (clock64() - t0 > limit_cycles) {
       if (err) atomicCAS(err, 0, code);
       return false;
     }
   }
+}
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* err, int code) {
+  return mbar_wait_limit(bar, parity, err, code, kWaitLimitCycles);
 }
 
 // 2D tiled TMA load (no multicast) into shared memory, completing `bytes` on `bar`.

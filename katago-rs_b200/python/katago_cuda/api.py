@@ -90,6 +90,7 @@ _SIGS = {
     "kc_copy_with_symmetry": ([FP, FP, I, I, I, I, I, I], I),
     "kc_gpool_fc": ([P, P, I, I, P, I, P, P], I),
     "kc_gpool_fc_noalloc": ([P, P, I, I, P, I, P, P], I),
+    "kc_selftest_device_timeout": ([P, I], I),
 }
 GPOOL_NOALLOC_MAX_FLOATS = 262144
 
@@ -246,6 +247,10 @@ class Handle:
 
     def synchronize(self, timeout_ms: int = 60000):
         _check(lib().kc_synchronize(self.h, timeout_ms))
+
+    def selftest_device_timeout(self, limit_us: int):
+        """kc_selftest_device_timeout: enqueue a kernel whose bounded wait runs out after `limit_us`."""
+        _check(lib().kc_selftest_device_timeout(self.h, limit_us))
 
     # ---- NeuralNet::get_output --------------------------------------------------------------------------------
     def get_output(self, spatial_rows, global_rows, meta_rows, symmetry, policy_optimism, want_ownership=True,

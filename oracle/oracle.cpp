@@ -731,9 +731,14 @@ static void forward(const Model& m, int N, const float* bin, const float* glob, 
           rms[i] = T(1) / den;
         }
       } else {
+        // ReduceSum over C x 361 terms: blocked (one partial per channel, then the partials), as a vectorised
+        // reduction sums, rather than one running float32 sum whose rounding error grows with the 277k terms
         T ss = 0;
-        for (int c = 0; c < C; c++)
-          for (int i = 0; i < S; i++) { T v = x[((size_t)n * C + c) * S + i]; ss += (v * v) * cx.mask[(size_t)n * S + i]; }
+        for (int c = 0; c < C; c++) {
+          T part = 0;
+          for (int i = 0; i < S; i++) { T v = x[((size_t)n * C + c) * S + i]; part += (v * v) * cx.mask[(size_t)n * S + i]; }
+          ss += part;
+        }
         T count = cx.mask_sum[n] * T(float(C));
         T ms = ss / count;
         T den = std::sqrt(ms + T(m.tip_eps));

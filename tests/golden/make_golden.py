@@ -50,6 +50,9 @@ NETS = {
     "b10c128": (2, (19,), 18, False),
     "b18c384nbt": (1, (19,), 19, False),
     "b10c384h6": (1, (19,), 20, False),
+    "tf3-b11c768": (2, (19, 13), 21, False),
+    "gqa-tf": (3, (19, 9, 13), 22, True),
+    "wide-nbt": (3, (13, 19, 9), 23, True),
 }
 
 

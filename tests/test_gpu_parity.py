@@ -84,14 +84,47 @@ def test_rows_are_independent(prec):
 
 
 def test_b18_full_batch():
-    """b18c384nbt at its benchmark batch (256, f16): every output finite, and sampled rows within 2e-2 of the
-    float32 oracle."""
+    """b18c384nbt at its benchmark batch (256 boards of 19x19, f16): every row against the float32 oracle (the
+    batch spans 400 pair tiles of 256 PBL rows, the last one ragged), and the batch reversed gives every row
+    bit-identical outputs (each row's arithmetic does not depend on which tile or CTA of the pair holds it)."""
     name = "b18c384nbt"
     spatial, glob, meta, _ = inputs.synthetic_inputs(256, 0xB200, (19,))
-    got = handle(name, kc.PRECISION_F16, 256).forward(spatial, glob)
+    h = handle(name, kc.PRECISION_F16, 256)
+    got = h.forward(spatial, glob)
     for k in KEYS:
         assert np.all(np.isfinite(got[k])), k
-    rows = [0, 101, 255]
+    want = OracleNet(netgen.net_bytes(name)).forward(spatial, glob)
+    errs = max_err(got, want)
+    assert max(errs.values()) <= 2e-2, errs
+    rev = h.forward(spatial[::-1].copy(), glob[::-1].copy())
+    for k in KEYS:
+        np.testing.assert_array_equal(rev[k][::-1], got[k])
+
+
+def test_b18_mixed_boards():
+    """The mixed-board configuration: b18c384nbt on 9x9 / 13x13 / 19x19 boards padded into 19x19 (masked BN,
+    masked mean and -1e4 max pooling at the benchmark widths), batch 64, f16, every row against the float32
+    oracle."""
+    name = "b18c384nbt"
+    spatial, glob, meta, sizes = inputs.synthetic_inputs(64, 0xB204, (9, 13, 19))
+    assert set(sizes.tolist()) == {9, 13, 19}
+    got = handle(name, kc.PRECISION_F16, 256).forward(spatial, glob)
+    want = OracleNet(netgen.net_bytes(name)).forward(spatial, glob)
+    errs = max_err(got, want)
+    assert max(errs.values()) <= 2e-2, errs
+
+
+def test_tf3_batch128():
+    """tf3-b11c768 at its benchmark batch (128, bf16 tier): 12 heads of 64 at width 768, fixed-theta RoPE, spatial
+    RMSNorm tip, 4 policy channels. Every output finite; 8 rows spread over the batch against the float32 oracle."""
+    name = "tf3-b11c768"
+    m = kc.Model(netgen.net_bytes(name))
+    spatial, glob, meta, _ = inputs.synthetic_inputs(128, 0xB203, (19, 13, 9), m.desc.num_input_channels,
+                                                     m.desc.num_input_global_channels)
+    got = handle(name, kc.PRECISION_BF16, 128).forward(spatial, glob)
+    for k in KEYS:
+        assert np.all(np.isfinite(got[k])), k
+    rows = [0, 1, 37, 63, 64, 100, 126, 127]
     want = OracleNet(netgen.net_bytes(name)).forward(spatial[rows], glob[rows])
     errs = {k: float(np.abs(got[k][rows] - want[k]).max()) for k in KEYS}
     assert max(errs.values()) <= 2e-2, errs
