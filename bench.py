@@ -319,11 +319,17 @@ class Runner:
         for _ in range(n):
             self.step()
             self.h.synchronize()
-        self.h.spatial[:self.args.batch] = self.spatial
-        self.h.glob[:self.args.batch] = self.glob
+        # e2e staging: each position's planes bit-packed once (the caller's input rows), symmetries drawn per row
+        from katago_cuda import api
+        b = self.args.batch
+        for i in range(b):
+            self.h.pk_bits[i] = api.pack_spatial(self.spatial[i])
+        self.h.pk_glob[:b] = self.glob
+        self.h.pk_sym[:b] = np.random.default_rng(self.gpu).integers(0, 8, size=b)
+        self.h.pk_opt[:b] = 0.0
         for _ in range(n):
-            self.h.enqueue(self.args.batch)
-            self.h.wait()
+            self.h.enqueue_packed(b, True)
+            self.h.wait_finished()
 
     def timed(self, k, profiled):
         """k steps on the handle's stream, each bracketed by CUDA events on that stream, L2 flushed before each
@@ -347,9 +353,11 @@ class Runner:
             return sum(ev_s[i].elapsed_time(ev_e[i]) for i in range(k)), prof
 
     def timed_e2e(self, k):
-        """k steps through the C ABI host path, timed by the host clock around kc_enqueue + kc_wait: the copy of
-        the pinned inputs to the device, the forward pass and the copy of every output row back, plus the host
-        side of both calls. L2 flushed before each step, outside the timed region."""
+        """k steps through the C ABI host path, timed by the host clock around kc_enqueue_packed + kc_wait: one
+        copy of the pinned bit-packed rows, symmetries and globals to the device, the forward pass with each row's
+        symmetry applied on the device, the reference's copy_outputs on the device, and the copy of every row's
+        NNOutput fields back, plus the host side of both calls. L2 flushed before each step, outside the timed
+        region."""
         import torch
         total = 0.0
         for _ in range(k):
@@ -357,8 +365,8 @@ class Runner:
             with torch.cuda.device(self.dev):
                 self.stream.synchronize()
             t0 = time.perf_counter()
-            self.h.enqueue(self.args.batch)
-            rows = self.h.wait()
+            self.h.enqueue_packed(self.args.batch, True)
+            rows = self.h.wait_finished()
             total += time.perf_counter() - t0
             if not np.isfinite(rows[0, 0]):
                 raise RuntimeError("non-finite output in the e2e run")
@@ -374,7 +382,7 @@ def run_ours(args):
     import torch
 
     import katago_cuda as kc
-    from katago_cuda import netgen
+    from katago_cuda import api, netgen
 
     rank, world, local = dist_env()
     dist = None
@@ -483,10 +491,11 @@ def run_ours(args):
             "flops_per_eval": flops_row,
             "model_tflops": flops_row * value / 1e12,
             "e2e": {"value": e2e_value, "unit": UNIT,
-                    "h2d_bytes_per_step": args.batch * (h.n_spatial + h.n_global) * 4,
-                    "d2h_bytes_per_step": args.batch * h.row_len * 4 + 4,
+                    "h2d_bytes_per_step": h.pk_bits.ctypes.data - h.pk_sym.ctypes.data + args.batch * h.pk_bits[0].nbytes,
+                    "d2h_bytes_per_step": args.batch * api.FINISHED_ROW_LEN * 4 + 4,
                     "ms_per_step": e2e_max_ms / args.steps,
-                    "timing": "host clock around kc_enqueue + kc_wait"},
+                    "timing": "host clock around kc_enqueue_packed(finish) + kc_wait: bit-packed rows in, device "
+                              "symmetry and copy_outputs, NNOutput rows out"},
             "gpu_launches": launches_per_step * args.steps,
             "clocks": clk,
         }

@@ -118,6 +118,45 @@ int kc_enqueue(kc_handle* h, int n);
  * reference waits on a helper thread (backend.rs:743-753); KC_ERR_TIMEOUT leaves the batch in flight. */
 int kc_wait(kc_handle* h, int timeout_ms, const float** out_rows);
 
+/* Bit-packed inputs. Every spatial input feature of the reference (nninputs.rs fill_row_v7 :1336) is 0 or 1, so a
+ * row's planes travel as bits: plane c of a row is KC_PACKED_WORDS_PER_PLANE 32-bit words, point p = y * 19 + x at bit
+ * p % 32 of word p / 32 (bits past 361 zero); 22 planes are 1,056 bytes instead of 31,768. Each row's symmetry is
+ * applied on the device as the planes are read (the inverse of SymmetryHelpers::copy_inputs_with_symmetry,
+ * nninputs.rs:872, which the reference runs on the host per row in copy_inputs, backend.rs:497-546). */
+#define KC_PACKED_WORDS_PER_PLANE 12
+
+/* NNOutput rows (the reference's copy_outputs, backend.rs:622-731, run on the device): per row KC_FINISHED_ROW_LEN
+ * floats: policy [362] (optimism mixed for v12+ nets, symmetry undone, pass last), value [3] (win, loss, noresult),
+ * misc [6] (scoreMean, scoreMeanSq, lead, varTimeLeft, shorttermWinlossError, shorttermScoreError, by model version),
+ * ownership [361] (symmetry undone). */
+#define KC_FINISHED_ROW_LEN 732
+#define KC_FINISHED_POLICY 0
+#define KC_FINISHED_VALUE 362
+#define KC_FINISHED_MISC 365
+#define KC_FINISHED_OWNERSHIP 371
+
+/* The handle's pinned staging for kc_enqueue_packed: spatial_bits [max_batch][C][KC_PACKED_WORDS_PER_PLANE],
+ * global [max_batch][G], meta [max_batch][M] (NULL when M = 0), symmetry [max_batch] (0..7: bit 0 flipY, bit 1
+ * flipX, bit 2 transpose), policy_optimism [max_batch]. The binding of BurnInputBuffers (backend.rs:150-212) for
+ * callers that write packed rows. */
+int kc_handle_packed_input_ptrs(kc_handle* h, uint32_t** spatial_bits, float** global, float** meta,
+                                int32_t** symmetry, float** policy_optimism);
+
+/* kc_enqueue for the packed staging: one host-to-device copy of rows [0, n), the forward pass with each row's
+ * symmetry applied on the device, and the readback. finish = 0 reads back the raw output rows (as kc_enqueue);
+ * finish = 1 runs the reference's copy_outputs on the device and reads back NNOutput rows of KC_FINISHED_ROW_LEN
+ * floats. kc_wait returns the rows of whichever the last enqueue read back. */
+int kc_enqueue_packed(kc_handle* h, int n, int finish);
+
+/* Pack one row's float planes [n_planes][361] into [n_planes][KC_PACKED_WORDS_PER_PLANE] words; KC_ERR_INVALID when a
+ * value is neither 0 nor 1. */
+int kc_pack_spatial(const float* planes, int n_planes, uint32_t* bits);
+
+/* The point mappings of the device-side symmetry, for tests of the host logic (no device is used): reverse = 0:
+ * table[y * 19 + x] = the input point the network sees at (y, x); reverse = 1: table[p] = the point an output p is
+ * moved to. Equal to kc_copy_with_symmetry's moves (nninputs.rs:756-831). */
+int kc_symmetry_table(int symmetry, int reverse, int* table);
+
 /* Same as kc_enqueue but the inputs and outputs are device pointers (no host copies): spatial [n,C,19,19],
  * global [n,G], meta [n,M] (may be NULL when M = 0), out [n,row_len] float32. For callers that keep their
  * batches on the GPU. */
@@ -134,7 +173,9 @@ int kc_synchronize(kc_handle* h, int timeout_ms);
 /* The whole reference get_output for one batch (backend.rs:410-731): per row, copy the inputs into the handle's
  * staging buffers with `symmetry[i]` (SymmetryHelpers::copy_inputs_with_symmetry, nninputs.rs:872), run the net,
  * then for each row mix the optimistic policy with `policy_optimism[i]` (v12+ nets), undo the symmetry on policy
- * and ownership, and write the NNOutput fields. Row inputs: `spatial_rows[i]` [C*19*19] NCHW,
+ * and ownership, and write the NNOutput fields. Rows travel bit-packed with the symmetry applied on the device when
+ * every spatial value is 0 or 1 (always, for the reference's inputs), else as floats with the symmetry applied on
+ * the host; the output handling runs on the device (kc_enqueue_packed with finish = 1). Row inputs: `spatial_rows[i]` [C*19*19] NCHW,
  * `global_rows[i]` [G], `meta_rows[i]` [M] (NULL when M = 0). Outputs per row i:
  *   policy_out + i*362 (362 floats, pass last), value_out + i*3 (win, loss, noresult),
  *   misc_out + i*6 (scoreMean, scoreMeanSq, lead, varTimeLeft, shorttermWinlossError, shorttermScoreError,

@@ -6,6 +6,7 @@
 // with its symmetry (:497-546), runs the net, then mixes policy optimism, undoes the symmetry and fills the score
 // fields by model version (:622-731).
 
+#include <algorithm>
 #include <chrono>
 #include <condition_variable>
 #include <cstdlib>
@@ -54,6 +55,21 @@ struct kc_handle {
   float* d_global = nullptr;
   float* d_meta = nullptr;
   float* d_out = nullptr;
+  // Bit-packed input staging: one pinned block and its device copy with the same layout, moved by one copy:
+  // [symmetry int32 x max_batch | optimism float x max_batch | global x max_batch G | meta x max_batch M |
+  //  spatial bits uint32 x max_batch C 12]
+  uint8_t* h_pk = nullptr;
+  uint8_t* d_pk = nullptr;
+  size_t pk_prefix = 0, pk_row_bits = 0;  // bytes before the bits; bytes of one row's bits
+  int32_t* pk_sym(uint8_t* base) const { return reinterpret_cast<int32_t*>(base); }
+  float* pk_opt(uint8_t* base) const { return reinterpret_cast<float*>(base + 4 * (size_t)max_batch); }
+  float* pk_global(uint8_t* base) const { return pk_opt(base) + max_batch; }
+  float* pk_meta(uint8_t* base) const { return pk_global(base) + (size_t)max_batch * n_global; }
+  uint32_t* pk_bits(uint8_t* base) const { return reinterpret_cast<uint32_t*>(base + pk_prefix); }
+  // NNOutput rows of the device copy_outputs: [max_batch][KC_FINISHED_ROW_LEN]
+  float* d_fin = nullptr;
+  float* h_fin = nullptr;
+  bool last_finished = false;  // the last enqueue read back NNOutput rows (h_fin) instead of raw rows (h_out)
   int last_n = 0;
   bool pending = false;
   std::vector<float> scratch;  // get_output: one row's symmetric copy
@@ -75,6 +91,10 @@ struct kc_handle {
     cudaFreeHost(h_meta);
     cudaFreeHost(h_out);
     cudaFreeHost(h_err);
+    cudaFreeHost(h_pk);
+    cudaFreeHost(h_fin);
+    cudaFree(d_pk);
+    cudaFree(d_fin);
     cudaFree(d_spatial);
     cudaFree(d_global);
     cudaFree(d_meta);
@@ -201,12 +221,16 @@ void wait_event(kc_handle* h, int timeout_ms) {
   }
 }
 
-void enqueue_host(kc_handle* h, int n) {
+void check_enqueue(kc_handle* h, int n) {
   if (n < 1 || n > h->max_batch)
     fail(KC_ERR_INVALID, "CUDA backend: batch of " + std::to_string(n) + " rows outside [1, " +
                              std::to_string(h->max_batch) + "]");
   if (h->pending) fail(KC_ERR_INVALID, "CUDA backend: kc_enqueue while the previous batch was not waited for");
   KC_CUDA(cudaSetDevice(h->device));
+}
+
+// Float planes: rows [0, n) of the pinned float inputs to the device.
+void upload_float(kc_handle* h, int n) {
   KC_CUDA(cudaMemcpyAsync(h->d_spatial, h->h_spatial, (size_t)n * h->n_spatial * sizeof(float), cudaMemcpyHostToDevice,
                           h->stream));
   KC_CUDA(cudaMemcpyAsync(h->d_global, h->h_global, (size_t)n * h->n_global * sizeof(float), cudaMemcpyHostToDevice,
@@ -214,12 +238,83 @@ void enqueue_host(kc_handle* h, int n) {
   if (h->n_meta)
     KC_CUDA(cudaMemcpyAsync(h->d_meta, h->h_meta, (size_t)n * h->n_meta * sizeof(float), cudaMemcpyHostToDevice,
                             h->stream));
-  h->engine->forward(n, h->stream, h->d_spatial, h->d_global, h->n_meta ? h->d_meta : nullptr, h->d_out);
-  const int row_len = h->engine->layout().row_len;
-  KC_CUDA(cudaMemcpyAsync(h->h_out, h->d_out, (size_t)n * row_len * sizeof(float), cudaMemcpyDeviceToHost, h->stream));
+}
+
+// Packed staging: symmetries, optimism, globals, meta and rows [0, n) of the bits in one copy (or the symmetries
+// and optimism alone).
+void upload_packed(kc_handle* h, int n, bool prefix_only) {
+  const size_t bytes = prefix_only ? (size_t)h->max_batch * 8 : h->pk_prefix + (size_t)n * h->pk_row_bits;
+  KC_CUDA(cudaMemcpyAsync(h->d_pk, h->h_pk, bytes, cudaMemcpyHostToDevice, h->stream));
+}
+
+void run_forward(kc_handle* h, int n, bool packed) {
+  if (packed)
+    h->engine->forward(n, h->stream, nullptr, h->pk_global(h->d_pk), h->n_meta ? h->pk_meta(h->d_pk) : nullptr,
+                       h->d_out, h->pk_bits(h->d_pk), h->pk_sym(h->d_pk));
+  else
+    h->engine->forward(n, h->stream, h->d_spatial, h->d_global, h->n_meta ? h->d_meta : nullptr, h->d_out);
+}
+
+// Read the batch back: the raw output rows, or (finish) the NNOutput rows of the device copy_outputs, which reads
+// the symmetries and optimism of the packed staging; then the device error word and the completion mark.
+void readback(kc_handle* h, int n, bool finish) {
+  if (finish) {
+    const kc::OutputLayout& L = h->engine->layout();
+    const kc::ModelDesc& m = h->model->desc;
+    kc::FinishParams fp;
+    fp.rows = h->d_out;
+    fp.row_len = L.row_len;
+    fp.policy_off = L.policy_off;
+    fp.value_off = L.value_off;
+    fp.score_off = L.score_off;
+    fp.own_off = L.own_off;
+    fp.P = m.num_policy_channels;
+    fp.version = m.version;
+    fp.has_own = m.num_ownership_channels() > 0;
+    fp.sym = h->pk_sym(h->d_pk);
+    fp.optimism = h->pk_opt(h->d_pk);
+    fp.out = h->d_fin;
+    kc::launch_finish_outputs(fp, n, h->stream);
+    KC_CUDA(cudaMemcpyAsync(h->h_fin, h->d_fin, (size_t)n * KC_FINISHED_ROW_LEN * sizeof(float),
+                            cudaMemcpyDeviceToHost, h->stream));
+  } else {
+    const int row_len = h->engine->layout().row_len;
+    KC_CUDA(cudaMemcpyAsync(h->h_out, h->d_out, (size_t)n * row_len * sizeof(float), cudaMemcpyDeviceToHost,
+                            h->stream));
+  }
   KC_CUDA(cudaMemcpyAsync(h->h_err, h->engine->error_word(), sizeof(int), cudaMemcpyDeviceToHost, h->stream));
   mark_batch(h);
   h->last_n = n;
+  h->last_finished = finish;
+}
+
+void enqueue_host(kc_handle* h, int n) {
+  check_enqueue(h, n);
+  upload_float(h, n);
+  run_forward(h, n, false);
+  readback(h, n, false);
+}
+
+// Pack one row's float planes [c][361] into c x 12 words (bit p % 32 of word p / 32 = point p); false if a value
+// is neither 0 nor 1 (the row then cannot travel packed).
+bool pack_row(const float* src, int c, uint32_t* dst) {
+  for (int k = 0; k < c; k++) {
+    const float* pl = src + (size_t)k * 361;
+    uint32_t* w = dst + (size_t)k * KC_PACKED_WORDS_PER_PLANE;
+    uint32_t bad = 0;
+    for (int j = 0; j < KC_PACKED_WORDS_PER_PLANE; j++) {
+      const int p0 = j * 32, cnt = std::min(32, 361 - p0);
+      uint32_t word = 0;
+      for (int i = 0; i < cnt; i++) {
+        const float v = pl[p0 + i];
+        word |= (uint32_t)(v != 0.0f) << i;
+        bad |= (uint32_t)(v != 0.0f && v != 1.0f);
+      }
+      w[j] = word;
+    }
+    if (bad) return false;
+  }
+  return true;
 }
 
 }  // namespace
@@ -382,6 +477,15 @@ int kc_handle_create(kc_context* ctx, int gpu_idx, int max_batch, int inputs_use
     KC_CUDA(cudaMalloc(&h->d_global, (size_t)max_batch * h->n_global * sizeof(float)));
     KC_CUDA(cudaMalloc(&h->d_meta, (size_t)max_batch * std::max(1, h->n_meta) * sizeof(float)));
     KC_CUDA(cudaMalloc(&h->d_out, (size_t)max_batch * row_len * sizeof(float)));
+    h->pk_prefix = ((size_t)max_batch * (2 + h->n_global + h->n_meta) * 4 + 255) / 256 * 256;
+    h->pk_row_bits = (size_t)m.num_input_channels * KC_PACKED_WORDS_PER_PLANE * 4;
+    const size_t pk_bytes = h->pk_prefix + (size_t)max_batch * h->pk_row_bits;
+    KC_CUDA(cudaMallocHost(&h->h_pk, pk_bytes));
+    std::memset(h->h_pk, 0, pk_bytes);
+    KC_CUDA(cudaMalloc(&h->d_pk, pk_bytes));
+    KC_CUDA(cudaMemset(h->d_pk, 0, pk_bytes));
+    KC_CUDA(cudaMallocHost(&h->h_fin, (size_t)max_batch * KC_FINISHED_ROW_LEN * sizeof(float)));
+    KC_CUDA(cudaMalloc(&h->d_fin, (size_t)max_batch * KC_FINISHED_ROW_LEN * sizeof(float)));
     h->scratch.resize(h->n_spatial);
     *out = h.release();
   });
@@ -427,7 +531,42 @@ int kc_wait(kc_handle* h, int timeout_ms, const float** out_rows) {
     if (!h->pending && h->last_n == 0) fail(KC_ERR_INVALID, "CUDA backend: kc_wait without kc_enqueue");
     KC_CUDA(cudaSetDevice(h->device));
     if (h->pending) wait_event(h, timeout_ms);
-    if (out_rows) *out_rows = h->h_out;
+    if (out_rows) *out_rows = h->last_finished ? h->h_fin : h->h_out;
+  });
+}
+
+int kc_handle_packed_input_ptrs(kc_handle* h, uint32_t** spatial_bits, float** global, float** meta,
+                                int32_t** symmetry, float** policy_optimism) {
+  return guard([&] {
+    need(h, "handle");
+    if (spatial_bits) *spatial_bits = h->pk_bits(h->h_pk);
+    if (global) *global = h->pk_global(h->h_pk);
+    if (meta) *meta = h->n_meta ? h->pk_meta(h->h_pk) : nullptr;
+    if (symmetry) *symmetry = h->pk_sym(h->h_pk);
+    if (policy_optimism) *policy_optimism = h->pk_opt(h->h_pk);
+  });
+}
+
+int kc_enqueue_packed(kc_handle* h, int n, int finish) {
+  return guard([&] {
+    need(h, "handle");
+    check_enqueue(h, n);
+    const int32_t* sym = h->pk_sym(h->h_pk);
+    for (int i = 0; i < n; i++)
+      if (sym[i] < 0 || sym[i] > 7) fail(KC_ERR_INVALID, "CUDA backend: symmetry " + std::to_string(sym[i]) + " outside [0, 8)");
+    upload_packed(h, n, false);
+    run_forward(h, n, true);
+    readback(h, n, finish != 0);
+  });
+}
+
+int kc_pack_spatial(const float* planes, int n_planes, uint32_t* bits) {
+  return guard([&] {
+    need(planes, "planes");
+    need(bits, "bits");
+    if (n_planes < 1) fail(KC_ERR_INVALID, "CUDA backend: no planes to pack");
+    if (!pack_row(planes, n_planes, bits))
+      fail(KC_ERR_INVALID, "CUDA backend: a spatial input value is neither 0 nor 1 and cannot be bit-packed");
   });
 }
 
@@ -481,59 +620,52 @@ int kc_get_output(kc_handle* h, int n, const float* const* spatial_rows, const f
     // the staging buffers below are still read by an earlier batch's copies while it is in flight
     if (h->pending) fail(KC_ERR_INVALID, "CUDA backend: kc_get_output while an enqueued batch was not waited for");
     const kc::ModelDesc& m = h->model->desc;
-    const int hw = 361;
-    // copy_inputs (backend.rs:497-546): symmetry and optimism are read here, before the batch runs
-    std::vector<int> sym(symmetry, symmetry + n);
-    std::vector<float> opt(policy_optimism, policy_optimism + n);
+    const int C = m.num_input_channels;
+    // copy_inputs (backend.rs:497-546): symmetry and optimism are read here, before the batch runs. Rows go to the
+    // device bit-packed, the symmetry applied there, unless a spatial value is neither 0 nor 1; then every row is
+    // copied as floats with its symmetry applied here, as the reference does.
+    int32_t* sym = h->pk_sym(h->h_pk);
+    float* opt = h->pk_opt(h->h_pk);
     for (int row = 0; row < n; row++) {
+      if (symmetry[row] < 0 || symmetry[row] > 7)
+        fail(KC_ERR_INVALID, "CUDA backend: symmetry " + std::to_string(symmetry[row]) + " outside [0, 8)");
+      sym[row] = symmetry[row];
+      opt[row] = policy_optimism[row];
       need(spatial_rows[row], "spatial row");
       need(global_rows[row], "global row");
-      std::memcpy(h->h_global + (size_t)row * h->n_global, global_rows[row], h->n_global * sizeof(float));
-      if (h->n_meta) {
-        if (!meta_rows || !meta_rows[row]) fail(KC_ERR_INVALID, "CUDA backend: model needs SGF metadata rows");
-        std::memcpy(h->h_meta + (size_t)row * h->n_meta, meta_rows[row], h->n_meta * sizeof(float));
-      }
-      copy_with_symmetry(spatial_rows[row], h->h_spatial + (size_t)row * h->n_spatial, 1, 19, 19,
-                         m.num_input_channels, sym[row], false);
+      if (h->n_meta && (!meta_rows || !meta_rows[row]))
+        fail(KC_ERR_INVALID, "CUDA backend: model needs SGF metadata rows");
     }
-    enqueue_host(h, n);
-    wait_event(h, timeout_ms);
-    // copy_outputs (backend.rs:622-731)
-    const kc::OutputLayout& L = h->engine->layout();
-    const int P = m.num_policy_channels;
-    std::vector<float> tmp(hw);
+    bool packed = true;
+    for (int row = 0; row < n && packed; row++)
+      packed = pack_row(spatial_rows[row], C, h->pk_bits(h->h_pk) + (size_t)row * C * KC_PACKED_WORDS_PER_PLANE);
+    float* glob = packed ? h->pk_global(h->h_pk) : h->h_global;
+    float* meta = packed ? h->pk_meta(h->h_pk) : h->h_meta;
     for (int row = 0; row < n; row++) {
-      const float* rd = h->h_out + (size_t)row * L.row_len;
-      const float* pol = rd + L.policy_off;
-      float* po = policy_out + (size_t)row * (hw + 1);
-      const float o = opt[row];
-      if (P == 2 || (P == 4 && m.version >= 16)) {
-        for (int i = 0; i < hw; i++) {
-          float p = pol[i], p_opt = pol[(hw + 1) + i];
-          tmp[i] = p + (p_opt - p) * o;
-        }
-        copy_with_symmetry(tmp.data(), po, 1, 19, 19, 1, sym[row], true);
-        po[hw] = pol[hw] + (pol[(hw + 1) + hw] - pol[hw]) * o;
-      } else {
-        copy_with_symmetry(pol, po, 1, 19, 19, 1, sym[row], true);
-        po[hw] = pol[hw];
-      }
-      const float* v = rd + L.value_off;
-      value_out[row * 3 + 0] = v[0];
-      value_out[row * 3 + 1] = v[1];
-      value_out[row * 3 + 2] = v[2];
-      if (ownership_out) copy_with_symmetry(rd + L.own_off, ownership_out + (size_t)row * hw, 1, 19, 19, 1, sym[row], true);
-      const float* s = rd + L.score_off;
-      float* mo = misc_out + (size_t)row * 6;
-      if (m.version >= 9) {
-        for (int i = 0; i < 6; i++) mo[i] = s[i];
-      } else if (m.version >= 8) {
-        mo[0] = s[0]; mo[1] = s[1]; mo[2] = s[2]; mo[3] = s[3]; mo[4] = 0; mo[5] = 0;
-      } else if (m.version >= 4) {
-        mo[0] = s[0]; mo[1] = s[1]; mo[2] = s[0]; mo[3] = 0; mo[4] = 0; mo[5] = 0;
-      } else {
-        mo[0] = s[0]; mo[1] = s[0] * s[0]; mo[2] = s[0]; mo[3] = 0; mo[4] = 0; mo[5] = 0;
-      }
+      std::memcpy(glob + (size_t)row * h->n_global, global_rows[row], h->n_global * sizeof(float));
+      if (h->n_meta) std::memcpy(meta + (size_t)row * h->n_meta, meta_rows[row], h->n_meta * sizeof(float));
+      if (!packed)
+        copy_with_symmetry(spatial_rows[row], h->h_spatial + (size_t)row * h->n_spatial, 1, 19, 19, C, sym[row],
+                           false);
+    }
+    KC_CUDA(cudaSetDevice(h->device));
+    if (packed) {
+      upload_packed(h, n, false);
+    } else {
+      upload_float(h, n);
+      upload_packed(h, n, true);  // the symmetries and optimism the device copy_outputs reads
+    }
+    run_forward(h, n, packed);
+    readback(h, n, true);
+    wait_event(h, timeout_ms);
+    // copy_outputs (backend.rs:622-731) ran on the device: each row's NNOutput fields are copied out
+    for (int row = 0; row < n; row++) {
+      const float* f = h->h_fin + (size_t)row * KC_FINISHED_ROW_LEN;
+      std::memcpy(policy_out + (size_t)row * 362, f + KC_FINISHED_POLICY, 362 * sizeof(float));
+      std::memcpy(value_out + (size_t)row * 3, f + KC_FINISHED_VALUE, 3 * sizeof(float));
+      std::memcpy(misc_out + (size_t)row * 6, f + KC_FINISHED_MISC, 6 * sizeof(float));
+      if (ownership_out)
+        std::memcpy(ownership_out + (size_t)row * 361, f + KC_FINISHED_OWNERSHIP, 361 * sizeof(float));
     }
   });
 }

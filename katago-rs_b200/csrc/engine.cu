@@ -306,6 +306,8 @@ struct Engine::Impl {
   int R = 0;
   int stem_rows = 0;
   const float* in_spatial = nullptr;
+  const uint32_t* in_bits = nullptr;  // bit-packed spatial planes (instead of in_spatial) and their symmetries
+  const int* in_sym = nullptr;
   const float* in_global = nullptr;
   const float* in_meta = nullptr;
   float* out = nullptr;
@@ -318,11 +320,18 @@ struct Engine::Impl {
   // Captured forward passes by (batch size and profiling, caller's buffers), least recently used first out of
   // `graph_lru` once more than kMaxGraphs are held (a caller that rotates buffers or batch sizes would otherwise
   // keep one graph per combination). An evicted graph that is still running is freed when it completes.
-  using GraphKey = std::tuple<int, const void*, const void*, const void*, void*>;
+  using GraphKey = std::tuple<int, const void*, const void*, const void*, const void*, const void*, void*>;
   static constexpr size_t kMaxGraphs = 64;
   std::map<GraphKey, std::pair<cudaGraphExec_t, uint64_t>> graphs;
   uint64_t graph_clock = 0;
 
+  InputSrc input() const {
+    InputSrc s;
+    s.f = in_bits ? nullptr : in_spatial;
+    s.bits = in_bits;
+    s.sym = in_sym;
+    return s;
+  }
   void* alloc(size_t bytes) {
     void* p = nullptr;
     KC_CUDA(cudaMalloc(&p, bytes));
@@ -1198,12 +1207,12 @@ struct Builder {
       T* pix = im2col ? reinterpret_cast<T*>(fbuffer(F_PIX, (grid_px * pix_c * (int)sizeof(T) + 3) / 4)) : nullptr;
       add(CLS_OTHER, [=](cudaStream_t st, int n) {
         if (im2col) {
-          launch_pdl(prep_pixels_kernel<T>, dim3((n * grid_px + 255) / 256), dim3(256), 0, st, Ip->in_spatial, n, cin,
+          launch_pdl(prep_pixels_kernel<T>, dim3((n * grid_px + 255) / 256), dim3(256), 0, st, Ip->input(), n, cin,
                      pad, pix, pix_c, Ip->rowmask);
           launch_pdl(prep_im2col_kernel<T>, dim3((n * 400 * (sk * sk + 1) + 255) / 256), dim3(256), 0, st,
                      (const T*)pix, n, sk, stem_dil, pad, pix_c, (T*)STEM.p, STEM.ld);
         } else
-          launch_pdl(prep_input_kernel<T>, dim3((n * 361 + 127) / 128), dim3(128), 0, st, Ip->in_spatial, n, cin,
+          launch_pdl(prep_input_kernel<T>, dim3((n * 361 + 127) / 128), dim3(128), 0, st, Ip->input(), n, cin,
                      (T*)STEM.p, STEM.ld, brows, stride, pad, Ip->rowmask);
       });
       BoardParams bp;
@@ -1226,6 +1235,7 @@ struct Builder {
       add(CLS_OTHER, [=](cudaStream_t st, int n) {
         BoardParams q = bp;
         q.spatial = Ip->in_spatial;
+        q.bits = Ip->in_bits;
         q.glob = Ip->in_global;
         q.meta = meta ? Ip->in_meta : nullptr;
         launch_pdl(board_kernel, dim3(n), dim3(256), 0, st, q);
@@ -1485,14 +1495,18 @@ void Engine::run_plan(int n, cudaStream_t stream, bool events) {
 }
 
 void Engine::forward(int n, cudaStream_t stream, const float* d_spatial, const float* d_global, const float* d_meta,
-                     float* d_out) {
+                     float* d_out, const uint32_t* d_bits, const int* d_sym) {
   if (n < 1 || n > max_batch_)
     fail(KC_ERR_INVALID, "CUDA backend: batch of " + std::to_string(n) + " rows outside [1, " +
                              std::to_string(max_batch_) + "]");
   Impl& I = *impl_;
   KC_CUDA(cudaSetDevice(device_));
   if (prof_pending_) collect_profile();
+  if (!d_bits == !d_spatial || (d_bits && !d_sym))
+    fail(KC_ERR_INVALID, "CUDA backend: a forward pass takes float planes or bit-packed planes with symmetries");
   I.in_spatial = d_spatial;
+  I.in_bits = d_bits;
+  I.in_sym = d_sym;
   I.in_global = d_global;
   I.in_meta = d_meta;
   I.out = d_out;
@@ -1500,8 +1514,8 @@ void Engine::forward(int n, cudaStream_t stream, const float* d_spatial, const f
   if (!use_graphs_) {
     run_plan(n, stream, events);
   } else {
-    auto key = std::make_tuple(n * 2 + (events ? 1 : 0), (const void*)d_spatial, (const void*)d_global,
-                               (const void*)d_meta, (void*)d_out);
+    auto key = std::make_tuple(n * 2 + (events ? 1 : 0), (const void*)d_spatial, (const void*)d_bits,
+                               (const void*)d_sym, (const void*)d_global, (const void*)d_meta, (void*)d_out);
     auto it = I.graphs.find(key);
     if (it == I.graphs.end()) {
       cudaGraph_t g;

@@ -11,6 +11,7 @@
 #include <vector>
 
 #include "model.h"
+#include "../../include/katago_cuda.h"
 
 namespace kc {
 
@@ -31,9 +32,10 @@ class Engine {
   Engine& operator=(const Engine&) = delete;
 
   // Enqueue the forward pass of n boards on `stream`: inputs and outputs are device pointers (NCHW float32 spatial
-  // [n][C][361], global [n][G], meta [n][192] or null; out [n][row_len] float32).
+  // [n][C][361], global [n][G], meta [n][192] or null; out [n][row_len] float32). Instead of d_spatial: bit-packed
+  // planes d_bits [n][C][12] with one symmetry per board d_sym [n], applied on the device.
   void forward(int n, cudaStream_t stream, const float* d_spatial, const float* d_global, const float* d_meta,
-               float* d_out);
+               float* d_out, const uint32_t* d_bits = nullptr, const int* d_sym = nullptr);
 
   const OutputLayout& layout() const { return layout_; }
   int max_batch() const { return max_batch_; }
@@ -72,6 +74,19 @@ class Engine {
   void run_plan(int n, cudaStream_t stream, bool events);
   void collect_profile();
 };
+
+// copy_outputs on the device (io.cu): the forward's raw output rows [n][row_len] -> NNOutput rows
+// [n][KC_FINISHED_ROW_LEN] (policy with the optimism mix and the inverse symmetry, value, misc by model version,
+// ownership with the inverse symmetry).
+struct FinishParams {
+  const float* rows = nullptr;
+  int row_len = 0, policy_off = 0, value_off = 0, score_off = 0, own_off = 0;
+  int P = 1, version = 0, has_own = 1;
+  const int* sym = nullptr;
+  const float* optimism = nullptr;
+  float* out = nullptr;
+};
+void launch_finish_outputs(const FinishParams& p, int n, cudaStream_t st);
 
 // Failure-detection self-test (ops.cu): enqueue on `st` one kernel whose bounded wait runs out after
 // `limit_cycles` SM cycles and records DEV_TIMEOUT_TEST in `err`.

@@ -5,18 +5,56 @@
 #pragma once
 
 #include "gemm.cuh"
+#include "../../include/katago_cuda.h"
 
 namespace kc {
 
 // Positions of a board in the padded board layout (PBL): row of (b, y, x) = b * 400 + (y + 1) * 20 + x.
 __host__ __device__ __forceinline__ int pbl_row(int b, int y, int x) { return b * 400 + (y + 1) * 20 + x; }
 
+// The point of a row's input that the network sees at (y, x) under `sym` (bit 0 flipY, bit 1 flipX, bit 2
+// transpose): the inverse of SymmetryHelpers::copy_inputs_with_symmetry's NCHW copy (nninputs.rs:756-831, 872),
+// which moves source point (h, w) to (h', w') = flipY/flipX of (h, w), transposed after the flips (with the flips
+// exchanged first when transposing).
+__host__ __device__ __forceinline__ int sym_src(int sym, int y, int x) {
+  const bool fy = (sym & 1) != 0, fx = (sym & 2) != 0;
+  int h, w;
+  if (sym & 4) {
+    w = fx ? 18 - y : y;
+    h = fy ? 18 - x : x;
+  } else {
+    h = fy ? 18 - y : y;
+    w = fx ? 18 - x : x;
+  }
+  return h * 19 + w;
+}
+
+// The spatial input of a forward pass: float32 planes [n][cin][361] in the reference layout, or bit-packed planes
+// [n][cin][12] (point p of a plane at bit p % 32 of word p / 32; every spatial feature of the reference's inputs is
+// 0 or 1, nninputs.rs fill_row_v7 :1336) with one symmetry per board applied as the planes are read.
+constexpr int kPackedWordsPerPlane = KC_PACKED_WORDS_PER_PLANE;
+struct InputSrc {
+  const float* f = nullptr;
+  const uint32_t* bits = nullptr;
+  const int* sym = nullptr;
+};
+
+// Plane c of board b at the network's (y, x).
+__device__ __forceinline__ float input_at(const InputSrc& in, int b, int cin, int c, int y, int x) {
+  if (in.bits) {
+    const int p = sym_src(__ldg(in.sym + b), y, x);
+    const uint32_t w = __ldg(in.bits + ((size_t)b * cin + c) * kPackedWordsPerPlane + (p >> 5));
+    return (float)((w >> (p & 31)) & 1u);
+  }
+  return __ldg(in.f + ((size_t)b * cin + c) * 361 + y * 19 + x);
+}
+
 // ---------------------------------------------------------------------------------------------------------------
 // Input: NCHW float32 [n][cin][19*19] -> stem layout T rows [b * brows + (y + pad) * stride + x][cpad], and the
 // per-PBL-row on-board mask (input channel 0, bin2onnx.py setup_mask :1203-1206).
 // ---------------------------------------------------------------------------------------------------------------
 template <typename T>
-__global__ void prep_input_kernel(const float* __restrict__ in, int n, int cin, T* __restrict__ out, int cpad,
+__global__ void prep_input_kernel(const __grid_constant__ InputSrc in, int n, int cin, T* __restrict__ out, int cpad,
                                   int brows, int stride, int pad, float* __restrict__ rowmask) {
   pdl_wait();
   pdl_trigger();
@@ -24,16 +62,15 @@ __global__ void prep_input_kernel(const float* __restrict__ in, int n, int cin, 
   if (idx >= n * 361) return;
   int b = idx / 361, pos = idx - b * 361;
   int y = pos / 19, x = pos - y * 19;
-  const float* src = in + (size_t)b * cin * 361 + pos;
   T* dst = out + ((size_t)b * brows + (size_t)(y + pad) * stride + x) * cpad;
   // cpad is a multiple of 8: the row is written as 16-byte vectors of 8 channels
   for (int c0 = 0; c0 < cpad; c0 += 8) {
     float v[8];
 #pragma unroll
-    for (int i = 0; i < 8; i++) v[i] = c0 + i < cin ? __ldg(src + (size_t)(c0 + i) * 361) : 0.0f;
+    for (int i = 0; i < 8; i++) v[i] = c0 + i < cin ? input_at(in, b, cin, c0 + i, y, x) : 0.0f;
     store_vec<T, 8>(dst + c0, v);
   }
-  rowmask[pbl_row(b, y, x)] = __ldg(src);
+  rowmask[pbl_row(b, y, x)] = input_at(in, b, cin, 0, y, x);
 }
 
 // ---------------------------------------------------------------------------------------------------------------
@@ -47,8 +84,8 @@ __global__ void prep_input_kernel(const float* __restrict__ in, int n, int cin, 
 // (row, tap) copying CP / 8 16-byte vectors; tap k * k zeroes the tail.
 // ---------------------------------------------------------------------------------------------------------------
 template <typename T>
-__global__ void prep_pixels_kernel(const float* __restrict__ in, int n, int cin, int pad, T* __restrict__ px, int cp,
-                                   float* __restrict__ rowmask) {
+__global__ void prep_pixels_kernel(const __grid_constant__ InputSrc in, int n, int cin, int pad, T* __restrict__ px,
+                                   int cp, float* __restrict__ rowmask) {
   pdl_wait();
   pdl_trigger();
   const int G = 19 + 2 * pad;
@@ -58,8 +95,23 @@ __global__ void prep_pixels_kernel(const float* __restrict__ in, int n, int cin,
   const int gy = q / G, gx = q - gy * G;
   const int y = gy - pad, x = gx - pad;
   const bool on = y >= 0 && y < 19 && x >= 0 && x < 19;
-  const float* src = in + (size_t)b * cin * 361 + (on ? y * 19 + x : 0);
   T* dst = px + (size_t)idx * cp;
+  if (on && in.bits) {
+    // one packed word per plane holds this point's bit
+    const int p = sym_src(__ldg(in.sym + b), y, x);
+    const uint32_t* wp = in.bits + (size_t)b * cin * kPackedWordsPerPlane + (p >> 5);
+    const int sh = p & 31;
+    for (int c0 = 0; c0 < cp; c0 += 8) {
+      float v[8];
+#pragma unroll
+      for (int i = 0; i < 8; i++)
+        v[i] = c0 + i < cin ? (float)((__ldg(wp + (size_t)(c0 + i) * kPackedWordsPerPlane) >> sh) & 1u) : 0.0f;
+      store_vec<T, 8>(dst + c0, v);
+      if (c0 == 0) rowmask[pbl_row(b, y, x)] = v[0];
+    }
+    return;
+  }
+  const float* src = in.f + (size_t)b * cin * 361 + (on ? y * 19 + x : 0);
   for (int c0 = 0; c0 < cp; c0 += 8) {
     float v[8];
 #pragma unroll
@@ -103,7 +155,8 @@ __global__ void prep_im2col_kernel(const T* __restrict__ px, int n, int k, int d
 // global features x initial matmul, plus the SGF-metadata encoder for human-SL nets (bin2onnx.py :1467-1487).
 // ---------------------------------------------------------------------------------------------------------------
 struct BoardParams {
-  const float* spatial;  // [n][cin][361] (channel 0 = mask)
+  const float* spatial;  // [n][cin][361] (channel 0 = mask), or null with bits
+  const uint32_t* bits;  // [n][cin][12] bit-packed planes (InputSrc), or null
   int cin;
   const float* glob;     // [n][G]
   int G;
@@ -126,7 +179,13 @@ static __global__ void board_kernel(const __grid_constant__ BoardParams p) {
   __shared__ float hbuf[2][512];
   const int b = blockIdx.x;
   float s = 0.0f;
-  for (int i = threadIdx.x; i < 361; i += blockDim.x) s += p.spatial[(size_t)b * p.cin * 361 + i];
+  if (p.bits) {
+    // plane 0 (the mask) as bits: the count of on-board points (a symmetry moves points, it does not change it)
+    if (threadIdx.x < kPackedWordsPerPlane)
+      s = (float)__popc(__ldg(p.bits + (size_t)b * p.cin * kPackedWordsPerPlane + threadIdx.x));
+  } else {
+    for (int i = threadIdx.x; i < 361; i += blockDim.x) s += p.spatial[(size_t)b * p.cin * 361 + i];
+  }
   red[threadIdx.x] = s;
   __syncthreads();
   for (int w = blockDim.x / 2; w > 0; w >>= 1) {

@@ -91,7 +91,14 @@ _SIGS = {
     "kc_gpool_fc": ([P, P, I, I, P, I, P, P], I),
     "kc_gpool_fc_noalloc": ([P, P, I, I, P, I, P, P], I),
     "kc_selftest_device_timeout": ([P, I], I),
+    "kc_handle_packed_input_ptrs": ([P, ctypes.POINTER(ctypes.POINTER(ctypes.c_uint32)), FPP, FPP,
+                                     ctypes.POINTER(ctypes.POINTER(ctypes.c_int32)), FPP], I),
+    "kc_enqueue_packed": ([P, I, I], I),
+    "kc_pack_spatial": ([FP, I, ctypes.POINTER(ctypes.c_uint32)], I),
+    "kc_symmetry_table": ([I, I, ctypes.POINTER(I)], I),
 }
+PACKED_WORDS_PER_PLANE = 12
+FINISHED_ROW_LEN, FINISHED_POLICY, FINISHED_VALUE, FINISHED_MISC, FINISHED_OWNERSHIP = 732, 0, 362, 365, 371
 GPOOL_NOALLOC_MAX_FLOATS = 262144
 
 
@@ -197,6 +204,14 @@ class Handle:
         _check(lib().kc_handle_output_layout(self.h, *[ctypes.byref(v) for v in vals]))
         self.row_len, self.policy_off, self.value_off, self.score_off, self.own_off = [v.value for v in vals]
         self.P = d.num_policy_channels
+        b, g, m, sy, op = (ctypes.POINTER(ctypes.c_uint32)(), FP(), FP(), ctypes.POINTER(ctypes.c_int32)(), FP())
+        _check(lib().kc_handle_packed_input_ptrs(self.h, ctypes.byref(b), ctypes.byref(g), ctypes.byref(m),
+                                                 ctypes.byref(sy), ctypes.byref(op)))
+        self.pk_bits = np.ctypeslib.as_array(b, shape=(max_batch, d.num_input_channels, PACKED_WORDS_PER_PLANE))
+        self.pk_glob = np.ctypeslib.as_array(g, shape=(max_batch, self.n_global))
+        self.pk_meta = np.ctypeslib.as_array(m, shape=(max_batch, self.n_meta)) if self.n_meta else None
+        self.pk_sym = np.ctypeslib.as_array(sy, shape=(max_batch,))
+        self.pk_opt = np.ctypeslib.as_array(op, shape=(max_batch,))
 
     def close(self):
         if getattr(self, "h", None):
@@ -236,6 +251,29 @@ class Handle:
             "scorevalue": rows[:, self.score_off:self.own_off],
             "ownership": rows[:, self.own_off:self.own_off + 361].reshape(n, 1, 19, 19),
         }
+
+    def enqueue_packed(self, n: int, finish: bool):
+        """kc_enqueue_packed: rows [0, n) of the packed staging (pk_bits, pk_glob, pk_meta, pk_sym, pk_opt)."""
+        _check(lib().kc_enqueue_packed(self.h, n, int(finish)))
+
+    def wait_finished(self, timeout_ms: int = 60000) -> np.ndarray:
+        """The NNOutput rows [max_batch, FINISHED_ROW_LEN] of the last kc_enqueue_packed(finish=1)."""
+        p = FP()
+        _check(lib().kc_wait(self.h, timeout_ms, ctypes.byref(p)))
+        return np.ctypeslib.as_array(p, shape=(self.max_batch, FINISHED_ROW_LEN))
+
+    def forward_packed(self, spatial, glob, symmetry, meta=None, timeout_ms: int = 120000) -> dict:
+        """Raw outputs (as forward) of n rows sent bit-packed with per-row symmetries applied on the device."""
+        n = spatial.shape[0]
+        for i in range(n):
+            self.pk_bits[i] = pack_spatial(spatial[i])
+        self.pk_glob[:n] = glob
+        if self.n_meta:
+            self.pk_meta[:n] = meta
+        self.pk_sym[:n] = symmetry
+        self.enqueue_packed(n, False)
+        rows = np.array(self.wait(timeout_ms)[:n])
+        return self.split(rows)
 
     def enqueue_device(self, n: int, d_spatial: int, d_global: int, d_meta: int, d_out: int):
         _check(lib().kc_enqueue_device(self.h, n, d_spatial, d_global, d_meta or None, d_out))
@@ -299,6 +337,21 @@ def gpool_fc(d_x: int, d_mask: int, n: int, c: int, d_w: int, oc: int, d_out: in
 def gpool_fc_noalloc(d_x: int, d_mask: int, n: int, c: int, d_w: int, oc: int, d_out: int, stream: int = 0):
     """kc_gpool_fc_noalloc: the same operator with its scratch in a fixed device array (no allocation)."""
     _check(lib().kc_gpool_fc_noalloc(d_x, d_mask, n, c, d_w, oc, d_out, stream or None))
+
+
+def pack_spatial(planes: np.ndarray) -> np.ndarray:
+    """kc_pack_spatial: float planes [C, 19, 19] of 0 / 1 -> [C, PACKED_WORDS_PER_PLANE] uint32."""
+    planes = np.ascontiguousarray(planes, np.float32)
+    c = planes.shape[0]
+    out = np.zeros((c, PACKED_WORDS_PER_PLANE), np.uint32)
+    _check(lib().kc_pack_spatial(_fp(planes), c, out.ctypes.data_as(ctypes.POINTER(ctypes.c_uint32))))
+    return out
+
+
+def symmetry_table(symmetry: int, reverse: bool) -> np.ndarray:
+    t = np.zeros(361, np.int32)
+    _check(lib().kc_symmetry_table(symmetry, int(reverse), t.ctypes.data_as(ctypes.POINTER(I))))
+    return t
 
 
 def copy_with_symmetry(src: np.ndarray, n: int, h: int, w: int, c: int, symmetry: int, reverse: bool) -> np.ndarray:
