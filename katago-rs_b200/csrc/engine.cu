@@ -174,10 +174,10 @@ struct PairMaps {
   CUtensorMap a, b, res, raw, act;
 };
 
-template <typename T, int BN, bool WIN, int MODE, bool RF32>
+template <typename T, int BN, bool WIN, int MODE, bool RF32, bool NORES = false>
 int launch_pair_bn(bool prepare, int pairs, cudaStream_t s, const PairMaps& m, const GemmParams& p) {
-  using C = PairCfg<BN, WIN, RF32>;
-  auto kernel = gemm_pair_kernel<T, BN, WIN, MODE, RF32>;
+  using C = PairCfg<BN, WIN, RF32, NORES>;
+  auto kernel = gemm_pair_kernel<T, BN, WIN, MODE, RF32, NORES>;
   cudaLaunchConfig_t cfg = {};
   cudaLaunchAttribute at[1];
   at[0].id = cudaLaunchAttributeClusterDimension;
@@ -209,7 +209,7 @@ int launch_pair_bn(bool prepare, int pairs, cudaStream_t s, const PairMaps& m, c
 
 // The pair kernel instances: tile width x (windowed 3x3 | linear | float32 residual | RoPE | SwiGLU), as chosen by
 // Impl::pair_tile.
-enum PairKind { PAIR_SEG = 0, PAIR_WIN = 1, PAIR_F32 = 2, PAIR_ROPE = 3, PAIR_SWIGLU = 4 };
+enum PairKind { PAIR_SEG = 0, PAIR_WIN = 1, PAIR_F32 = 2, PAIR_ROPE = 3, PAIR_SWIGLU = 4, PAIR_SEG_NORES = 5 };
 
 template <typename T>
 int launch_pair(bool prepare, int bn, int kind, int pairs, cudaStream_t s, const PairMaps& m, const GemmParams& p) {
@@ -219,6 +219,10 @@ int launch_pair(bool prepare, int bn, int kind, int pairs, cudaStream_t s, const
     case PAIR_SEG * 1000 + 128: return launch_pair_bn<T, 128, false, MODE_SEGMENTS, false>(prepare, pairs, s, m, p);
     case PAIR_SEG * 1000 + 192: return launch_pair_bn<T, 192, false, MODE_SEGMENTS, false>(prepare, pairs, s, m, p);
     case PAIR_SEG * 1000 + 256: return launch_pair_bn<T, 256, false, MODE_SEGMENTS, false>(prepare, pairs, s, m, p);
+    case PAIR_SEG_NORES * 1000 + 64: return launch_pair_bn<T, 64, false, MODE_SEGMENTS, false, true>(prepare, pairs, s, m, p);
+    case PAIR_SEG_NORES * 1000 + 128: return launch_pair_bn<T, 128, false, MODE_SEGMENTS, false, true>(prepare, pairs, s, m, p);
+    case PAIR_SEG_NORES * 1000 + 192: return launch_pair_bn<T, 192, false, MODE_SEGMENTS, false, true>(prepare, pairs, s, m, p);
+    case PAIR_SEG_NORES * 1000 + 256: return launch_pair_bn<T, 256, false, MODE_SEGMENTS, false, true>(prepare, pairs, s, m, p);
     case PAIR_WIN * 1000 + 64: return launch_pair_bn<T, 64, true, MODE_SEGMENTS, false>(prepare, pairs, s, m, p);
     case PAIR_WIN * 1000 + 128: return launch_pair_bn<T, 128, true, MODE_SEGMENTS, false>(prepare, pairs, s, m, p);
     case PAIR_WIN * 1000 + 192: return launch_pair_bn<T, 192, true, MODE_SEGMENTS, false>(prepare, pairs, s, m, p);
@@ -676,8 +680,14 @@ struct Builder {
         pm.res = box(res);
         pm.raw = box(raw);
         pm.act = box(act);
+        // linears and 1x1 convolutions without a residual: the instance without residual boxes (a deeper pipeline;
+        // KATAGO_CUDA_PAIR_NORES=0: the general one)
+        const char* nr = std::getenv("KATAGO_CUDA_PAIR_NORES");
+        bool any_res = false;
+        for (int i = 0; i < p.nseg; i++) any_res = any_res || (p.seg[i].flags & EPI_RESIDUAL);
+        const bool nores = !any_res && !(nr && nr[0] == '0');
         const int kind = s.mode == MODE_ROPE ? PAIR_ROPE : s.mode == MODE_SWIGLU ? PAIR_SWIGLU : pf32 ? PAIR_F32
-                         : pwin ? PAIR_WIN : PAIR_SEG;
+                         : pwin ? PAIR_WIN : nores ? PAIR_SEG_NORES : PAIR_SEG;
         if (kind == PAIR_ROPE) {
           p.rope_cos = s.rope_cos_rows;
           p.rope_sin = s.rope_sin_rows;
@@ -688,7 +698,8 @@ struct Builder {
         // when that spreads a launch over more SM pairs than it adds tile rounds (KATAGO_CUDA_PAIR_NARROW=0: off).
         // A tile costs about its width plus a fixed ~74 columns' worth (prologue, pipeline fill, epilogue).
         const char* ne = std::getenv("KATAGO_CUDA_PAIR_NARROW");
-        const bool narrow = (kind == PAIR_SEG || kind == PAIR_WIN) && pbn > 64 && s.N % 64 == 0 && !(ne && ne[0] == '0');
+        const bool narrow = (kind == PAIR_SEG || kind == PAIR_SEG_NORES || kind == PAIR_WIN) && pbn > 64 && s.N % 64 == 0 &&
+                            !(ne && ne[0] == '0');
         PairMaps pm64 = pm;
         int max_pairs64 = 0;
         if (narrow) {

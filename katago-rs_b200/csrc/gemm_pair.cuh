@@ -32,7 +32,9 @@ namespace kc {
 // window travels with its chunk's first stage, on that stage's barrier: no barriers of its own. Slot ch % 2 is free
 // when that stage's slot is (its MMAs follow chunk ch - 2's whenever STAGES <= 4, with 3 stages per chunk). This cuts the TMA bytes of a
 // 3x3 convolution's K-block from 28 KB to about 14 KB per CTA, below what TMA delivers per SM.
-template <int BN, bool WIN = false, bool RF32 = false>
+// NORES: the tile has no residual input, so its epilogue warps need no residual boxes; the shared memory goes to
+// pipeline stages instead (the 1x1 convolutions without a residual: a third stage).
+template <int BN, bool WIN = false, bool RF32 = false, bool NORES = false>
 struct PairCfg {
   static_assert(BN % 64 == 0 && BN >= 64 && BN <= 256, "pair tile width");
   static_assert(!(WIN && RF32), "float32 residual tiles are linears");
@@ -62,7 +64,7 @@ struct PairCfg {
   static constexpr int BOX_BYTES = 32 * 32 * 2;
   static constexpr int RBOX_BYTES = RF32 ? 32 * 32 * 4 : BOX_BYTES;  // raw output and residual boxes
   static constexpr int ABOX_BYTES = RF32 ? 0 : BOX_BYTES;            // act output box (none with RF32)
-  static constexpr int NRES = WIN || RF32 || BN > 128 ? 2 : 4;  // residual boxes in flight per epilogue warp
+  static constexpr int NRES = NORES ? 0 : WIN || RF32 || BN > 128 ? 2 : 4;  // residual boxes in flight per warp
   static constexpr int EPI_WARP_BYTES = RBOX_BYTES + ABOX_BYTES + NRES * RBOX_BYTES;  // raw, act, residual ring
   static constexpr int EPI_BYTES = EPI_WARPS * EPI_WARP_BYTES;
   static constexpr int PARAM_COLS = 768;          // per-column BN scale / bias in shared memory
@@ -202,12 +204,12 @@ __device__ __forceinline__ void pair_act(const float (&v)[32], const float* sc, 
   }
 }
 
-template <typename T, int BN, bool WIN, int MODE = MODE_SEGMENTS, bool RF32 = false>
-__global__ void __launch_bounds__(PairCfg<BN, WIN, RF32>::THREADS, 1)
+template <typename T, int BN, bool WIN, int MODE = MODE_SEGMENTS, bool RF32 = false, bool NORES = false>
+__global__ void __launch_bounds__(PairCfg<BN, WIN, RF32, NORES>::THREADS, 1)
     gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                      const __grid_constant__ CUtensorMap tmRes, const __grid_constant__ CUtensorMap tmRaw,
                      const __grid_constant__ CUtensorMap tmAct, const __grid_constant__ GemmParams p) {
-  using C = PairCfg<BN, WIN, RF32>;
+  using C = PairCfg<BN, WIN, RF32, NORES>;
   static_assert(MODE != MODE_ROPE || C::WARP_COLS == 64, "RoPE tiles give each epilogue warp one head of 64");
   static_assert(MODE != MODE_ROPE || (C::NRES * C::RBOX_BYTES >= 4096 && C::RBOX_BYTES + C::ABOX_BYTES == 4096),
                 "RoPE table rows: cos in the residual ring, sin in the raw and act staging boxes");
@@ -464,7 +466,7 @@ __global__ void __launch_bounds__(PairCfg<BN, WIN, RF32>::THREADS, 1)
     uint8_t* st_act = wbuf + C::RBOX_BYTES;  // RoPE: the head's second rotation half
     constexpr int RES_OFF = C::RBOX_BYTES + C::ABOX_BYTES;  // the residual ring after the raw and act boxes
     uint64_t* rb = rbar + C::NRES * ew;
-    const bool has_res = (flags & EPI_RESIDUAL) != 0;  // one-segment GEMMs only
+    const bool has_res = !NORES && (flags & EPI_RESIDUAL) != 0;  // one-segment GEMMs only
     const int a0 = p.seg[0].act, a1 = p.nseg > 1 ? p.seg[1].act : a0;
     const int res_x = p.pair_res_x, raw_x = p.pair_raw_x, act_x = p.pair_act_x;
     const uint32_t tempty_leader0 = mapa_shared(smem_u32(&tempty[0]), 0);
