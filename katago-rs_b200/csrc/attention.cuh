@@ -4,7 +4,9 @@
 //
 // One CTA per (head, board). A board's 400 PBL rows (361 points plus zero halo rows) are the keys, so every key of
 // the board is in one tile and the softmax is a single exact pass, no online rescaling. K [416 x 64] and
-// V [448 x 64] are loaded once (128B-swizzled TMA boxes) and the board's queries run as four 128-row tiles.
+// V [448 x 64] are loaded once (128B-swizzled TMA boxes) and the board's queries run as three 128-row tiles from
+// the board's row 20 (rows 0..19 are the halo row above the board, no query): rows 20..403 cover every point
+// (rows 400..403 belong to the next board and are neither kept nor written).
 // Sixteen warps, four per TMEM lane quarter, each one query row per thread and a quarter of the keys:
 //   S = Q K^T (M = 128, N = 2 x 208, K = 64) into TMEM [0, 416);
 //   row max over S (exchanged in shared memory), p = 2^((s - max) * scale * log2 e) for on-board keys (0 for
@@ -36,7 +38,8 @@ struct AttnParams {
 struct AttnCfg {
   static constexpr int KEYS = 416;         // S columns: the board's 400 rows padded to 2 x 208
   static constexpr int PKEYS = 448;        // P / V keys: 7 x 64
-  static constexpr int QTILES = 4;         // 128-row query tiles covering the board's 400 rows
+  static constexpr int QTILES = 3;         // 128-row query tiles covering the board's rows 20..399
+  static constexpr int QROW0 = 20;         // first query row: the board's first point
   static constexpr int K_OFF = 0;
   static constexpr int K_BYTES = KEYS * 128;           // 53248
   static constexpr int V_OFF = K_OFF + K_BYTES;
@@ -184,7 +187,7 @@ __global__ void __launch_bounds__(AttnCfg::THREADS, 1)
     tma_load_2d(smem + C::V_OFF, &tmV, kv_full, p.qc + p.kc + kvh * 64, row0);
     tma_load_2d(smem + C::V_OFF + 224 * 128, &tmV, kv_full, p.qc + p.kc + kvh * 64, row0 + 224);
     mbar_expect_tx(q_full, C::Q_BYTES);
-    tma_load_2d(smem + C::Q_OFF, &tmQ, q_full, h * 64, row0);
+    tma_load_2d(smem + C::Q_OFF, &tmQ, q_full, h * 64, row0 + C::QROW0);
     cok = mbar_wait(kv_full, 0, p.err, DEV_TIMEOUT_MMA);
     issue_s(0);
   }
@@ -202,9 +205,9 @@ __global__ void __launch_bounds__(AttnCfg::THREADS, 1)
   bool ok = true;
   for (int t = 0; t < C::QTILES; t++) {
     const uint32_t ph = t & 1;
-    const int qrow = t * 128 + r;  // query row within the board
+    const int qrow = C::QROW0 + t * 128 + r;  // query row within the board
     // the quarter's warps whose 32 rows are all past the board's 400 rows only keep the barrier protocol
-    const bool live = t * 128 + q * 32 < 400;
+    const bool live = C::QROW0 + t * 128 + q * 32 < 400;
     const float mq = qrow < 400 ? __ldg(p.rowmask + row0 + qrow) : 0.0f;  // for the output, loaded early
     ok = ok && mbar_wait(s_full, ph, p.err, DEV_TIMEOUT_EPILOGUE);
     __syncwarp();
@@ -260,7 +263,7 @@ __global__ void __launch_bounds__(AttnCfg::THREADS, 1)
         umma_commit(pa_free);
         if (t + 1 < C::QTILES) {
           mbar_expect_tx(q_full, C::Q_BYTES);
-          tma_load_2d(smem + C::Q_OFF, &tmQ, q_full, h * 64, row0 + (t + 1) * 128);
+          tma_load_2d(smem + C::Q_OFF, &tmQ, q_full, h * 64, row0 + C::QROW0 + (t + 1) * 128);
         }
       }
     }
