@@ -8,11 +8,10 @@
 
 #include <algorithm>
 #include <chrono>
-#include <condition_variable>
 #include <cstdlib>
 #include <cstring>
 #include <memory>
-#include <mutex>
+#include <thread>
 #include <string>
 #include <vector>
 
@@ -72,11 +71,13 @@ struct kc_handle {
   bool last_finished = false;  // the last enqueue read back NNOutput rows (h_fin) instead of raw rows (h_out)
   int last_n = 0;
   bool pending = false;
+  // host time of the last completion mark and a running estimate of how long a batch takes from there, per batch
+  // size class: a waiter sleeps through most of that and polls the rest
+  std::chrono::steady_clock::time_point t_mark;
+  double est_us[2] = {0.0, 0.0};  // batches of up to / above half the maximum
+  bool mark_is_batch = false;     // the last mark follows a forward pass (kc_synchronize's marks do not count)
+
   std::vector<float> scratch;  // get_output: one row's symmetric copy
-  // completion: a host function enqueued behind each batch counts it done and wakes the waiter (no polling)
-  std::mutex mu;
-  std::condition_variable cv;
-  uint64_t enq_seq = 0, done_seq = 0;
 
   ~kc_handle() {
     if (stream) {
@@ -175,43 +176,45 @@ void check_device(int dev) {
                                ") is not an sm_100 (Blackwell B200) GPU");
 }
 
-void CUDART_CB on_batch_done(void* arg) {
-  kc_handle* h = static_cast<kc_handle*>(arg);
-  {
-    std::lock_guard<std::mutex> lock(h->mu);
-    h->done_seq++;
-  }
-  h->cv.notify_all();
-}
-
-// Record completion of everything enqueued so far on the handle's stream: an event (for error queries) and a host
-// function that wakes wait_event.
-void mark_batch(kc_handle* h) {
+// Record completion of everything enqueued so far on the handle's stream (`batch`: behind a forward pass).
+void mark_batch(kc_handle* h, bool batch = true) {
   KC_CUDA(cudaEventRecord(h->done, h->stream));
-  {
-    std::lock_guard<std::mutex> lock(h->mu);
-    h->enq_seq++;
-  }
-  KC_CUDA(cudaLaunchHostFunc(h->stream, on_batch_done, h));
+  h->t_mark = std::chrono::steady_clock::now();
+  h->mark_is_batch = batch;
   h->pending = true;
 }
 
+// Wait for the last mark: sleep through 85% of the estimated batch time, then poll the event, yielding the thread
+// between queries (a few microseconds from completion to return, and no spinning for most of the batch); past the
+// estimate, poll every 20 us. timeout_ms < 0: no limit.
 void wait_event(kc_handle* h, int timeout_ms) {
-  bool finished;
-  {
-    std::unique_lock<std::mutex> lock(h->mu);
-    auto done = [&] { return h->done_seq >= h->enq_seq; };
-    if (timeout_ms < 0) {
-      h->cv.wait(lock, done);
-      finished = true;
-    } else {
-      finished = h->cv.wait_for(lock, std::chrono::milliseconds(timeout_ms), done);
-    }
+  using clock = std::chrono::steady_clock;
+  const auto t0 = clock::now();
+  const int cls = h->last_n > h->max_batch / 2 ? 1 : 0;
+  const double est = h->mark_is_batch ? h->est_us[cls] : 0.0;
+  const auto deadline = t0 + std::chrono::milliseconds(timeout_ms < 0 ? 0 : timeout_ms);
+  if (est > 0) {
+    auto wake = h->t_mark + std::chrono::microseconds((long long)(0.8 * est));
+    if (timeout_ms >= 0 && wake > deadline) wake = deadline;
+    if (wake > t0 && cudaEventQuery(h->done) == cudaErrorNotReady) std::this_thread::sleep_until(wake);
   }
-  cudaError_t e = cudaEventQuery(h->done);
-  if (e != cudaSuccess && e != cudaErrorNotReady) KC_CUDA(e);
-  if (!finished)
-    fail(KC_ERR_TIMEOUT, "CUDA backend: batch did not finish within " + std::to_string(timeout_ms) + " ms");
+  while (true) {
+    cudaError_t e = cudaEventQuery(h->done);
+    if (e == cudaSuccess) break;
+    if (e != cudaErrorNotReady) KC_CUDA(e);
+    const auto now = clock::now();
+    if (timeout_ms >= 0 && now > deadline)
+      fail(KC_ERR_TIMEOUT, "CUDA backend: batch did not finish within " + std::to_string(timeout_ms) + " ms");
+    const double since_mark = std::chrono::duration<double, std::micro>(now - h->t_mark).count();
+    if (est <= 0 || since_mark < 1.5 * est + 200) std::this_thread::yield();
+    else std::this_thread::sleep_for(std::chrono::microseconds(20));
+  }
+  // the estimate follows a shorter batch at once (oversleeping costs latency) and a longer one slowly (a batch
+  // held up by other work on the stream moves it by at most a factor 1.1)
+  if (h->mark_is_batch) {
+    const double took = std::chrono::duration<double, std::micro>(clock::now() - h->t_mark).count();
+    h->est_us[cls] = est <= 0 || took < est ? took : 0.9 * est + 0.1 * std::min(took, 2.0 * est);
+  }
   h->pending = false;
   if (*h->h_err != 0) {
     int code = *h->h_err;
@@ -599,7 +602,7 @@ int kc_synchronize(kc_handle* h, int timeout_ms) {
   return guard([&] {
     need(h, "handle");
     KC_CUDA(cudaSetDevice(h->device));
-    mark_batch(h);
+    mark_batch(h, false);
     wait_event(h, timeout_ms);
   });
 }
@@ -707,7 +710,7 @@ int kc_selftest_device_timeout(kc_handle* h, int limit_us) {
     const long long cycles = (long long)limit_us * (khz > 0 ? khz : 2000000) / 1000;
     kc::launch_wait_selftest(h->engine->error_word(), cycles, h->stream);
     KC_CUDA(cudaMemcpyAsync(h->h_err, h->engine->error_word(), sizeof(int), cudaMemcpyDeviceToHost, h->stream));
-    mark_batch(h);
+    mark_batch(h, false);
   });
 }
 

@@ -225,7 +225,7 @@ class Handle:
     def enqueue(self, n: int):
         _check(lib().kc_enqueue(self.h, n))
 
-    def wait(self, timeout_ms: int = 60000) -> np.ndarray:
+    def wait(self, timeout_ms: int = -1) -> np.ndarray:
         """The n output rows of the last enqueue (a view of pinned memory, valid until the next enqueue)."""
         p = FP()
         _check(lib().kc_wait(self.h, timeout_ms, ctypes.byref(p)))
@@ -256,7 +256,7 @@ class Handle:
         """kc_enqueue_packed: rows [0, n) of the packed staging (pk_bits, pk_glob, pk_meta, pk_sym, pk_opt)."""
         _check(lib().kc_enqueue_packed(self.h, n, int(finish)))
 
-    def wait_finished(self, timeout_ms: int = 60000) -> np.ndarray:
+    def wait_finished(self, timeout_ms: int = -1) -> np.ndarray:
         """The NNOutput rows [max_batch, FINISHED_ROW_LEN] of the last kc_enqueue_packed(finish=1)."""
         p = FP()
         _check(lib().kc_wait(self.h, timeout_ms, ctypes.byref(p)))
@@ -283,7 +283,7 @@ class Handle:
         _check(lib().kc_handle_stream(self.h, ctypes.byref(s)))
         return s.value or 0
 
-    def synchronize(self, timeout_ms: int = 60000):
+    def synchronize(self, timeout_ms: int = -1):
         _check(lib().kc_synchronize(self.h, timeout_ms))
 
     def selftest_device_timeout(self, limit_us: int):
