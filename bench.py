@@ -277,7 +277,7 @@ def run_reference(args):
                                    "C++ restatement in oracle/ (float32, OpenMP on all host threads)"},
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
-    print(json.dumps(line), flush=True)
+    print_line(json.dumps(line))
 
 
 class Runner:
@@ -506,19 +506,49 @@ def run_ours(args):
                                               "CPU oracle float32 (reference arithmetic restated in C++, an "
                                               "unoptimised restatement, not the reference's flex backend), "
                                               "OpenMP on all host threads"}
-        print(json.dumps(line), flush=True)
+        print_line(json.dumps(line))
     for r in runners:
         r.h.close()
     if dist:
         dist.destroy_process_group()
 
 
+class StdoutToStderr:
+    """Points file descriptor 1 at stderr while the run's libraries may print there (NCCL prints its version banner
+    when the first collective builds the communicator), so that stdout carries only the bench's JSON line."""
+
+    def __enter__(self):
+        sys.stdout.flush()
+        self.saved = os.dup(1)
+        os.dup2(2, 1)
+        self.out = os.fdopen(os.dup(self.saved), "w")
+        return self
+
+    def emit(self, line):
+        self.out.write(line + "\n")
+        self.out.flush()
+
+    def __exit__(self, *exc):
+        sys.stdout.flush()
+        os.dup2(self.saved, 1)
+        os.close(self.saved)
+        self.out.close()
+        return False
+
+
 def main():
     args = parse()
-    if args.impl == "reference":
-        run_reference(args)
-    else:
-        run_ours(args)
+    global print_line
+    with StdoutToStderr() as guard:
+        print_line = guard.emit
+        if args.impl == "reference":
+            run_reference(args)
+        else:
+            run_ours(args)
+
+
+def print_line(line):
+    print(line, flush=True)
 
 
 if __name__ == "__main__":
