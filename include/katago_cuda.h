@@ -76,6 +76,9 @@ int kc_device_count(int* count);
 
 /* Parse a KataGo model file (.bin, .bin.gz, .txt, .txt.gz) from memory. `file_name` (may be NULL) decides text vs
  * binary floats as the reference does (bin2onnx.py:1074-1082); NULL means: binary if the data holds "@BIN@".
+ * A name ending in ".onnx" (or, without a name, data that starts as an ONNX ModelProto) is read as the ONNX export
+ * the reference's tools/bin2onnx/bin2onnx.py writes (the files the reference's burn backend is generated from,
+ * crates/katago-nn-burn/build.rs:25-30): its layers are rebuilt from the graph and its metadata_props.
  * Replaces NeuralNet::load_model_file (nninterface.rs:137; backend.rs:277-292). No device is touched. */
 int kc_model_load(const void* bytes, size_t n, const char* file_name, kc_model** out);
 

@@ -349,6 +349,7 @@ int kc_model_load(const void* bytes, size_t n, const char* file_name, kc_model**
     need(out, "out");
     *out = nullptr;
     int binary = -1;
+    bool onnx = false;
     if (file_name) {
       std::string f(file_name);
       for (auto& c : f) c = (char)std::tolower((unsigned char)c);
@@ -357,10 +358,16 @@ int kc_model_load(const void* bytes, size_t n, const char* file_name, kc_model**
         return f.size() >= k && f.compare(f.size() - k, k, s) == 0;
       };
       binary = (ends(".txt") || ends(".txt.gz")) ? 0 : 1;
+      onnx = ends(".onnx");
+    } else {
+      // an ONNX ModelProto starts with its ir_version field (tag 0x08); a KataGo file starts with its name (text) or
+      // the gzip magic
+      onnx = n > 16 && static_cast<const uint8_t*>(bytes)[0] == 0x08;
     }
     try {
       auto m = std::make_unique<kc_model>();
-      m->desc = kc::parse_model(static_cast<const uint8_t*>(bytes), n, binary);
+      m->desc = onnx ? kc::parse_onnx(static_cast<const uint8_t*>(bytes), n)
+                     : kc::parse_model(static_cast<const uint8_t*>(bytes), n, binary);
       *out = m.release();
     } catch (const Error& e) {
       fail(e.status, std::string("Error loading or parsing model file ") + (file_name ? file_name : "<memory>") + ": " +

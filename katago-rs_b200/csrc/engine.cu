@@ -243,6 +243,12 @@ int launch_pair(bool prepare, int bn, int kind, int pairs, cudaStream_t s, const
 // cos/sin of the float32 angle evaluated in float64 and rounded).
 void rope_tables(const BlockDesc& b, std::vector<float>& cs, std::vector<float>& sn, int& tables) {
   const int half = b.head_dim / 2, P = half;
+  if (!b.rope_cos.empty()) {  // tables stored in the file
+    tables = b.rope_ntables;
+    cs = b.rope_cos;
+    sn = b.rope_sin;
+    return;
+  }
   if (b.learnable_rope) {
     tables = b.kv_heads;
     cs.assign((size_t)tables * 361 * half, 0.0f);

@@ -376,6 +376,7 @@ bool ModelDesc::has_any_nested_bottleneck_blocks() const {
 }
 
 int64_t ModelDesc::num_parameters() const {
+  if (arch_num_parameters >= 0) return arch_num_parameters;
   int64_t n = np_conv(initial_conv) + np_mm(initial_matmul);
   if (has_meta) n += np_mm(meta_mul1) + np_mb(meta_bias1) + np_mm(meta_mul2) + np_mb(meta_bias2) + np_mm(meta_mul3);
   for (auto& b : blocks) n += np_block(b);
@@ -387,7 +388,9 @@ int64_t ModelDesc::num_parameters() const {
   return n;
 }
 
-double ModelDesc::trunk_spatial_conv_depth() const { return depth_conv(initial_conv) + depth_stack(blocks); }
+double ModelDesc::trunk_spatial_conv_depth() const {
+  return arch_conv_depth >= 0 ? arch_conv_depth : depth_conv(initial_conv) + depth_stack(blocks);
+}
 
 ModelDesc parse_model(const uint8_t* data, size_t n, int binary_floats) {
   std::vector<uint8_t> inflated;

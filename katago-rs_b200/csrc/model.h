@@ -60,6 +60,10 @@ struct BlockDesc {
   bool use_rope = false, learnable_rope = false;
   float rope_theta = 0;
   std::vector<float> rope_freqs;  // [kv_heads][head_dim/2][2]
+  // RoPE tables as a file stores them (ONNX models): [rope_ntables][361][head_dim / 2] cos and sin; empty: the
+  // engine computes them from rope_freqs / rope_theta
+  std::vector<float> rope_cos, rope_sin;
+  int rope_ntables = 0;
   TfRmsDesc ln;
   MatMulDesc q, k, v, out;
   int ffn = 0;
@@ -117,7 +121,15 @@ struct ModelDesc {
   bool has_any_nested_bottleneck_blocks() const;
   int64_t num_parameters() const;
   double trunk_spatial_conv_depth() const;
+  // the architecture summary a file states (ONNX metadata numParameters / trunkSpatialConvDepth, written because a
+  // graph has no layer list to recompute them from); < 0: computed from the layers
+  int64_t arch_num_parameters = -1;
+  double arch_conv_depth = -1;
 };
+
+// Parse a KataGo net exported as ONNX by the reference's tools/bin2onnx/bin2onnx.py (the graph GraphBuilder emits,
+// :1088-1615, and its metadata_props): the layer list is rebuilt from the graph. Throws kc::Error(KC_ERR_PARSE, ...).
+ModelDesc parse_onnx(const uint8_t* data, size_t n);
 
 // Parse a model file held in memory. `binary_floats` selects "@BIN@" float blocks (.bin) or text floats (.txt).
 // gzip data is detected by its magic bytes and inflated first. Throws kc::Error(KC_ERR_PARSE, ...) on failure.
