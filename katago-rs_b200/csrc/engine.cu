@@ -207,6 +207,23 @@ int launch_pair_bn(bool prepare, int pairs, cudaStream_t s, const PairMaps& m, c
   return pairs;
 }
 
+// How a pair launch of `tiles` tiles of width `w` runs on at most `P` pairs: how many pairs, from which work item on
+// tiles are column halves (`split`: when the last, partly filled round of tiles then fits one round of half items),
+// and its cost in column units: a tile costs about its width plus a fixed ~74 columns' worth (prologue, pipeline
+// fill, epilogue), a round the cost of its largest item.
+struct PairPlan {
+  int pairs, split_from;
+  long long cost;
+};
+PairPlan plan_pair(int tiles, int P, int w, bool split) {
+  const int rounds = tiles / P, rem = tiles % P;
+  if (split && rem > 0 && 2 * rem <= P) {
+    if (rounds == 0) return {2 * rem, 0, w / 2 + 74};
+    return {P, rounds * P, rounds * (w + 74LL) + (w / 2 + 74)};
+  }
+  return {std::min(tiles, P), 1 << 30, (long long)((tiles + P - 1) / P) * (w + 74)};
+}
+
 // The pair kernel instances: tile width x (windowed 3x3 | linear | float32 residual | RoPE | SwiGLU), as chosen by
 // Impl::pair_tile.
 enum PairKind { PAIR_SEG = 0, PAIR_WIN = 1, PAIR_F32 = 2, PAIR_ROPE = 3, PAIR_SWIGLU = 4, PAIR_SEG_NORES = 5 };
@@ -680,12 +697,6 @@ struct Builder {
           p.win_rows = round_up(128 + 2 * halo, 8);
           if (p.win_rows > PairCfg<256, true>::WIN_MAX_ROWS) pwin = false;
         }
-        PairMaps pm;
-        pm.a = make_map(s.A.p, ebf, s.A.ld, a_rows, pwin ? p.win_rows : 128);
-        pm.b = make_map(dW, ebf, K, s.N, pbn / 2);
-        pm.res = box(res);
-        pm.raw = box(raw);
-        pm.act = box(act);
         // linears and 1x1 convolutions without a residual: the instance without residual boxes (a deeper pipeline;
         // KATAGO_CUDA_PAIR_NORES=0: the general one)
         const char* nr = std::getenv("KATAGO_CUDA_PAIR_NORES");
@@ -694,6 +705,13 @@ struct Builder {
         const bool nores = !any_res && !(nr && nr[0] == '0');
         const int kind = s.mode == MODE_ROPE ? PAIR_ROPE : s.mode == MODE_SWIGLU ? PAIR_SWIGLU : pf32 ? PAIR_F32
                          : pwin ? PAIR_WIN : nores ? PAIR_SEG_NORES : PAIR_SEG;
+        const bool kwin = kind == PAIR_WIN, knores = kind == PAIR_SEG_NORES;
+        PairMaps pm;
+        pm.a = make_map(s.A.p, ebf, s.A.ld, a_rows, pwin ? p.win_rows : 128);
+        pm.b = make_map(dW, ebf, K, s.N, pair_b_box_rows(pbn, kwin, knores));
+        pm.res = box(res);
+        pm.raw = box(raw);
+        pm.act = box(act);
         if (kind == PAIR_ROPE) {
           p.rope_cos = s.rope_cos_rows;
           p.rope_sin = s.rope_sin_rows;
@@ -709,24 +727,27 @@ struct Builder {
         PairMaps pm64 = pm;
         int max_pairs64 = 0;
         if (narrow) {
-          pm64.b = make_map(dW, ebf, K, s.N, 32);
+          pm64.b = make_map(dW, ebf, K, s.N, pair_b_box_rows(64, kwin, knores));
           max_pairs64 = launch_pair<E>(true, 64, kind, 0, 0, pm64, p);
         }
+        // windowed and residual-free tiles: the last, partly filled round as column halves (KATAGO_CUDA_PAIR_SPLIT=0:
+        // off)
+        const char* se = std::getenv("KATAGO_CUDA_PAIR_SPLIT");
+        const bool split = pair_split_tiles(pbn, kwin, knores) && !(se && se[0] == '0');
         add(s.cls, [=](cudaStream_t st, int n) {
           GemmParams q = p;
           q.g.rows = n * brows;
           const int mt = (q.g.rows + 255) / 256;
-          const int tiles = mt * (q.n_total / pbn);
+          const PairPlan pl = plan_pair(mt * (q.n_total / pbn), max_pairs, pbn, split);
           if (narrow) {
-            const int tiles64 = mt * (q.n_total / 64);
-            const long long cost = (long long)((tiles + max_pairs - 1) / max_pairs) * (pbn + 74);
-            const long long cost64 = (long long)((tiles64 + max_pairs64 - 1) / max_pairs64) * (64 + 74);
-            if (cost64 < cost) {
-              launch_pair<E>(false, 64, kind, std::min(tiles64, max_pairs64), st, pm64, q);
+            const PairPlan pl64 = plan_pair(mt * (q.n_total / 64), max_pairs64, 64, false);
+            if (pl64.cost < pl.cost) {
+              launch_pair<E>(false, 64, kind, pl64.pairs, st, pm64, q);
               return;
             }
           }
-          launch_pair<E>(false, pbn, kind, std::min(tiles, max_pairs), st, pm, q);
+          q.split_from = pl.split_from;
+          launch_pair<E>(false, pbn, kind, pl.pairs, st, pm, q);
         });
         return;
       }
@@ -812,13 +833,17 @@ struct Builder {
     g.act_c0 = c0;
     return g;
   }
-  // residual-closing segment: y = acc (* mask) + X; X = y; XA = act(next(y))
-  Seg close_seg(int width, Tensor X, Tensor XA, BnAct next, bool mask_acc) {
+  // residual-closing segment: y = acc (* mask) + X; X = y; XA = act(next(y)). raw_live false: nothing reads X
+  // after this block (the last block of a nested block's inner stack, whose closing 1x1 reads only XA), so y is
+  // not written back when XA is (2-byte residual streams).
+  Seg close_seg(int width, Tensor X, Tensor XA, BnAct next, bool mask_acc, bool raw_live = true) {
     Seg g;
     g.width = width;
-    g.flags = EPI_RESIDUAL | EPI_RAW | (mask_acc ? EPI_MASK_ACC : 0) | (X.f32 ? EPI_RES_F32 | EPI_RAW_F32 : 0);
+    const bool raw = raw_live || !next.bn || X.f32;
+    g.flags = EPI_RESIDUAL | (raw ? EPI_RAW : 0) | (mask_acc ? EPI_MASK_ACC : 0) |
+              (X.f32 ? EPI_RES_F32 | EPI_RAW_F32 : 0);
     g.res = X;
-    g.raw = X;
+    if (raw) g.raw = X;
     if (next.bn) {
       g.flags |= EPI_ACT;
       g.act = next.act;
@@ -916,11 +941,13 @@ struct Builder {
   }
 
   // ---- blocks ----
-  void emit_stack(const std::vector<BlockDesc>& v, int depth, int C, BnAct after) {
-    for (size_t i = 0; i < v.size(); i++) emit_block(v[i], depth, C, consumer_bn(v, i + 1, after));
+  // raw_live: whether the stack's residual stream is read after its last block
+  void emit_stack(const std::vector<BlockDesc>& v, int depth, int C, BnAct after, bool raw_live = true) {
+    for (size_t i = 0; i < v.size(); i++)
+      emit_block(v[i], depth, C, consumer_bn(v, i + 1, after), i + 1 < v.size() || raw_live);
   }
 
-  void emit_block(const BlockDesc& b, int depth, int C, BnAct next) {
+  void emit_block(const BlockDesc& b, int depth, int C, BnAct next, bool raw_live = true) {
     Tensor X = tensor(R_LEVEL0 + 2 * depth, C);
     Tensor XA = tensor(R_LEVEL0 + 2 * depth + 1, C);
     if (b.kind == BLOCK_ORDINARY) {
@@ -928,7 +955,7 @@ struct Builder {
       Tensor T1 = tensor(R_T1, b.regular.oc);
       gemm(conv_spec(CLS_CONV3, XA, C, {&b.regular}, {act_seg(w16(b.regular.oc), b.mid_bn, b.mid_act, T1)}));
       gemm(conv_spec(b.final_conv.ky == 3 ? CLS_CONV3 : CLS_LINEAR, T1, b.final_conv.ic, {&b.final_conv},
-                     {close_seg(w16(C), X, XA, next, false)}));
+                     {close_seg(w16(C), X, XA, next, false, raw_live)}));
     } else if (b.kind == BLOCK_GPOOL) {
       // bin2onnx.py gpool_block :1250-1261: regular and gpool convs share one GEMM
       const int rc = b.regular.oc, gc = b.gpool_conv.oc;
@@ -944,7 +971,7 @@ struct Builder {
       pool(G, 0, gc, false, pooled);
       fc(pooled, 3 * gc, b.gpool_to_bias, nullptr, ACT_IDENTITY, gbias, rc, 0, 1);
       bias_bnact(REG, 0, gbias, b.mid_bn, b.mid_act, rc, T1);
-      gemm(conv_spec(CLS_CONV3, T1, rc, {&b.final_conv}, {close_seg(w16(C), X, XA, next, false)}));
+      gemm(conv_spec(CLS_CONV3, T1, rc, {&b.final_conv}, {close_seg(w16(C), X, XA, next, false, raw_live)}));
     } else if (b.kind == BLOCK_NESTED) {
       // bin2onnx.py nested_bottleneck_block :1263-1269
       const int mid = b.pre_conv.oc;
@@ -963,8 +990,8 @@ struct Builder {
         s.actout = MA;
       }
       gemm(conv_spec(CLS_LINEAR, XA, C, {&b.pre_conv}, {s}));
-      emit_stack(b.inner, depth + 1, mid, {&b.post_bn, b.post_act});
-      gemm(conv_spec(CLS_LINEAR, MA, mid, {&b.post_conv}, {close_seg(w16(C), X, XA, next, false)}));
+      emit_stack(b.inner, depth + 1, mid, {&b.post_bn, b.post_act}, false);
+      gemm(conv_spec(CLS_LINEAR, MA, mid, {&b.post_conv}, {close_seg(w16(C), X, XA, next, false, raw_live)}));
     } else if (b.kind == BLOCK_ATTENTION) {
       emit_attention(b, X, XA, C, next);
     } else {

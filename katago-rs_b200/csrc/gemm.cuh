@@ -92,6 +92,11 @@ struct alignas(16) GemmParams {
   int* err = nullptr;
   // windowed A (CTA-pair kernel, 3x3 convolutions): one window of win_rows rows starting halo rows above the tile
   int halo = 0, win_rows = 0;
+  // CTA-pair kernel, windowed tiles of width >= 128: work items from split_from on are column halves of the tiles
+  // from split_from on (two items per tile), so that a last, partly filled round of tiles becomes one round of
+  // half-width items on up to twice as many pairs. Honoured only when every pair gets at most one half item, as its
+  // last item: split_from a multiple of the launched pairs and 2 x (tiles - split_from) <= pairs.
+  int split_from = 1 << 30;
   // CTA-pair kernel: columns >= pair_split belong to segment 1; the x coordinate of an output / residual box is
   // pair_*_x + GEMM column (the segment's c0 minus its first column)
   int pair_split = 0, pair_raw_x = 0, pair_act_x = 0, pair_res_x = 0;

@@ -26,6 +26,14 @@
 
 namespace kc {
 
+// Tiles that may run as column halves: windowed 3x3 tiles and residual-free 1x1 tiles of width >= 128. Rows of one
+// TMA load of their weights (B): half of a CTA's BH rows (a whole tile loads both halves, a half tile one), BH
+// otherwise.
+__host__ __device__ constexpr bool pair_split_tiles(int bn, bool win, bool nores) { return (win || nores) && bn >= 128; }
+__host__ __device__ constexpr int pair_b_box_rows(int bn, bool win, bool nores) {
+  return pair_split_tiles(bn, win, nores) ? bn / 4 : bn / 2;
+}
+
 // WIN (3x3 convolutions, 9 taps): per 64-channel chunk, each CTA loads one A window (its 128 rows plus the taps'
 // halo above and below) into one of two window slots, and every tap's MMA reads its 128 rows at the tap's row offset
 // inside the window; the pipeline stages carry the weight boxes (three taps per stage: 12 MMAs per wait). The
@@ -34,6 +42,10 @@ namespace kc {
 // 3x3 convolution's K-block from 28 KB to about 14 KB per CTA, below what TMA delivers per SM.
 // NORES: the tile has no residual input, so its epilogue warps need no residual boxes; the shared memory goes to
 // pipeline stages instead (the 1x1 convolutions without a residual: a third stage).
+// SPLIT (pair_split_tiles): the tiles of a launch's last, partly filled round may run as column halves
+// (MMAs of N = BN / 2 on the same accumulator, one weight box per K-block instead of two, the epilogue warps' boxes
+// shared out over the half), one half per pair, so that the round takes about half a tile's time on up to twice
+// as many pairs (GemmParams::split_from).
 template <int BN, bool WIN = false, bool RF32 = false, bool NORES = false>
 struct PairCfg {
   static_assert(BN % 64 == 0 && BN >= 64 && BN <= 256, "pair tile width");
@@ -41,6 +53,9 @@ struct PairCfg {
   static constexpr int BH = BN / 2;               // B rows (output columns) staged by each CTA of the pair
   static constexpr int A_BYTES = 128 * 64 * 2;    // one 64-channel K-block of this CTA's 128 rows
   static constexpr int B_BYTES = BH * 64 * 2;     // one K-block of this CTA's half of the weights
+  static constexpr bool SPLIT = pair_split_tiles(BN, WIN, NORES);  // work items may be column halves of tiles
+  static constexpr int BBOX = pair_b_box_rows(BN, WIN, NORES);     // weight rows per TMA load
+  static constexpr int HALF_CHUNKS = BN / 64;               // 32-column boxes of a half tile
   static constexpr int KB_BYTES = (WIN ? 0 : A_BYTES) + B_BYTES;  // one K-block's slot in a stage
   static constexpr int KBS = WIN ? 3 : 2;         // K-blocks per pipeline stage (WIN: a row of three taps)
   static constexpr int WIN_TAPS = 9;
@@ -52,11 +67,13 @@ struct PairCfg {
   // the tile's columns; the windowed 3x3 keeps 2 (its third weight stage is worth more), and so do float32
   // residual tiles (their boxes are twice as large). With 12 epilogue warps
   // the CTA has 16 (512 threads, 128 registers each at launch) and setmaxnreg moves registers from warpgroup 0
-  // (TMA producer, MMA issuer, two idle warps: 56 each) to the three epilogue warpgroups (152 each):
-  // 4 x 32 x 56 + 12 x 32 x 152 = 65,536, and per SMSP 56 + 3 x 152 = 512 x 32 = 16,384.
+  // (TMA producer, MMA issuer, two idle warps: 48 each) to the three epilogue warpgroups (152 each):
+  // 4 x 32 x 48 + 12 x 32 x 152 = 64,512 <= 65,536, per SMSP 48 + 3 x 152 = 504 <= 4 x 128. (With 56 for
+  // warpgroup 0 the compiler spilled in the residual 1x1 instance; with 48 it does not.)
   static constexpr int EPI_WARPS = BN == 192 && !WIN && !RF32 ? 12 : 8;
   static constexpr int EPI_WARP0 = EPI_WARPS == 12 ? 4 : 2;  // first epilogue warp (a warpgroup boundary with 12)
-  static constexpr int WG0_REGS = 56, EPI_REGS = 152;
+  static constexpr int WG0_REGS = 48, EPI_REGS = 152;
+  static_assert(WG0_REGS + 3 * EPI_REGS <= 4 * 128 && WG0_REGS % 8 == 0 && EPI_REGS % 8 == 0, "register split");
   static constexpr int WARP_COLS = BN / (EPI_WARPS / 4);
   static constexpr int CHUNKS = WARP_COLS / 32;   // 32-column boxes per warp and tile
   // staging boxes of 32 rows x 32 columns: 2-byte outputs in 64-byte rows (64-byte swizzle), float32 raw outputs
@@ -262,6 +279,24 @@ __global__ void __launch_bounds__(PairCfg<BN, WIN, RF32, NORES>::THREADS, 1)
   const int kb_per_tap = p.cin / 64;
   const int KB = p.taps * kb_per_tap;
   const int NST = (KB + C::KBS - 1) / C::KBS;
+  // work items: tiles [0, sf) whole, then two column halves per tile (SPLIT); each pair takes items pair,
+  // pair + npairs, ... and so at most one half item, its last
+  int sf = num_tiles;
+  if constexpr (C::SPLIT) {
+    if (p.split_from < num_tiles && p.split_from % npairs == 0 && 2 * (num_tiles - p.split_from) <= npairs)
+      sf = p.split_from;
+  }
+  const int num_items = sf + 2 * (num_tiles - sf);
+  // item -> tile and column half (-1: the whole tile)
+  auto item_tile = [&](int it, int& hf) {
+    if (!C::SPLIT || it < sf) {
+      hf = -1;
+      return it;
+    }
+    hf = (it - sf) & 1;
+    return sf + ((it - sf) >> 1);
+  };
+  constexpr uint32_t IDESC_HALF = make_idesc_f16(fmt, 256, C::SPLIT ? BN / 2 : BN);
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < C::STAGES; s++) {
@@ -309,23 +344,32 @@ __global__ void __launch_bounds__(PairCfg<BN, WIN, RF32, NORES>::THREADS, 1)
         *abort_flag = 1;
         return false;
       };
-      for (int tile = pair; tile < num_tiles && ok; tile += npairs) {
+      for (int it = pair; it < num_items && ok; it += npairs) {
+        int hf;
+        const int tile = item_tile(it, hf);
         const int m0 = (tile / n_tiles) * 256 + (int)rank * 128;
-        const int nb = (tile % n_tiles) * BN + (int)rank * C::BH;
+        // this CTA's weight rows: half of the tile's columns, or (half item) half of the item's BN / 2
+        const int nb = (tile % n_tiles) * BN + (hf < 0 ? (int)rank * C::BH : hf * (BN / 2) + (int)rank * (BN / 4));
         if constexpr (WIN) {
+          const uint32_t b_bytes = hf < 0 ? C::B_BYTES : C::B_BYTES / 2;
           for (int ch = 0; ch < kb_per_tap && ok; ch++) {
             for (int t0 = 0; t0 < C::WIN_TAPS; t0 += C::KBS) {
               if (!(ok = slot_free(&empty[stage], phase ^ 1))) break;
               const uint32_t win_bytes = t0 == 0 ? (uint32_t)p.win_rows * 128u : 0u;
-              if (leader) mbar_expect_tx(&full[stage], 2u * (C::KBS * C::B_BYTES + win_bytes));
+              if (leader) mbar_expect_tx(&full[stage], 2u * (C::KBS * b_bytes + win_bytes));
               const uint32_t fb = mapa_shared(smem_u32(&full[stage]), 0);
               if (t0 == 0) {  // the chunk's A window rides on its first stage
                 tma_load_2d_pair(awin + as * C::A_WIN_BYTES, &tmA, fb, ch * 64, m0 - p.halo);
                 as ^= 1;
               }
-              for (int j = 0; j < C::KBS; j++)
-                tma_load_2d_pair(stages + stage * C::STAGE_BYTES + j * C::KB_BYTES, &tmB, fb,
-                                 (t0 + j) * p.cin + ch * 64, nb);
+              for (int j = 0; j < C::KBS; j++) {
+                uint8_t* dst = stages + stage * C::STAGE_BYTES + j * C::KB_BYTES;
+                const int x = (t0 + j) * p.cin + ch * 64;
+                tma_load_2d_pair(dst, &tmB, fb, x, nb);
+                // a whole tile's second weight box: the rows after the first, where one box of BH rows would put
+                // them (BBOX rows of 128 bytes = whole 1024-byte swizzle atoms)
+                if (C::SPLIT && hf < 0) tma_load_2d_pair(dst + C::BBOX * 128, &tmB, fb, x, nb + C::BBOX);
+              }
               if (++stage == C::STAGES) {
                 stage = 0;
                 phase ^= 1;
@@ -333,19 +377,22 @@ __global__ void __launch_bounds__(PairCfg<BN, WIN, RF32, NORES>::THREADS, 1)
             }
           }
         } else {
+          const uint32_t kb_bytes = hf < 0 ? C::KB_BYTES : C::A_BYTES + C::B_BYTES / 2;
           for (int st = 0; st < NST; st++) {
             if (!(ok = slot_free(&empty[stage], phase ^ 1))) break;
             const int kb0 = st * C::KBS;
             const int nk = KB - kb0 < C::KBS ? KB - kb0 : C::KBS;
-            if (leader) mbar_expect_tx(&full[stage], 2u * (uint32_t)nk * C::KB_BYTES);
+            if (leader) mbar_expect_tx(&full[stage], 2u * (uint32_t)nk * kb_bytes);
             const uint32_t fb = mapa_shared(smem_u32(&full[stage]), 0);
             uint8_t* sbase = stages + stage * C::STAGE_BYTES;
             for (int j = 0; j < nk; j++) {
               const int kb = kb0 + j;
               const int tap = kb / kb_per_tap;
               const int c0 = (kb - tap * kb_per_tap) * 64;
+              uint8_t* dst = sbase + j * C::KB_BYTES + C::A_BYTES;
               tma_load_2d_pair(sbase + j * C::KB_BYTES, &tmA, fb, c0, m0 + s_params->tap_off[tap]);
-              tma_load_2d_pair(sbase + j * C::KB_BYTES + C::A_BYTES, &tmB, fb, kb * 64, nb);
+              tma_load_2d_pair(dst, &tmB, fb, kb * 64, nb);
+              if (C::SPLIT && hf < 0) tma_load_2d_pair(dst + C::BBOX * 128, &tmB, fb, kb * 64, nb + C::BBOX);
             }
             if (++stage == C::STAGES) {
               stage = 0;
@@ -377,7 +424,10 @@ __global__ void __launch_bounds__(PairCfg<BN, WIN, RF32, NORES>::THREADS, 1)
       uint32_t win_off[C::WIN_TAPS];
 #pragma unroll
       for (int t = 0; t < C::WIN_TAPS; t++) win_off[t] = WIN ? (uint32_t)(p.halo + s_params->tap_off[t]) * 128u : 0u;
-      for (int tile = pair; tile < num_tiles && ok; tile += npairs, local++) {
+      for (int it = pair; it < num_items && ok; it += npairs, local++) {
+        int hf;
+        item_tile(it, hf);
+        const uint32_t idesc = hf < 0 ? IDESC : IDESC_HALF;  // a half item: N = BN / 2
         const int acc = local & 1;
         const uint32_t acc_phase = (local >> 1) & 1;
         if (!mbar_wait(&tempty[acc], acc_phase ^ 1, p.err, DEV_TIMEOUT_MMA) || *abort_flag) {
@@ -411,7 +461,7 @@ __global__ void __launch_bounds__(PairCfg<BN, WIN, RF32, NORES>::THREADS, 1)
                 const uint32_t sb = sbase + j * C::KB_BYTES;
 #pragma unroll
                 for (int k = 0; k < 4; k++)
-                  umma_f16_pair(d_tmem, make_sw128_desc(sa + k * 32), make_sw128_desc(sb + k * 32), IDESC,
+                  umma_f16_pair(d_tmem, make_sw128_desc(sa + k * 32), make_sw128_desc(sb + k * 32), idesc,
                                 (ch | g | j | k) != 0);
               }
               release(&empty[stage]);
@@ -432,7 +482,7 @@ __global__ void __launch_bounds__(PairCfg<BN, WIN, RF32, NORES>::THREADS, 1)
               const uint32_t sa = sbase + j * C::KB_BYTES, sb = sa + C::A_BYTES;
 #pragma unroll
               for (int k = 0; k < 4; k++)
-                umma_f16_pair(d_tmem, make_sw128_desc(sa + k * 32), make_sw128_desc(sb + k * 32), IDESC,
+                umma_f16_pair(d_tmem, make_sw128_desc(sa + k * 32), make_sw128_desc(sb + k * 32), idesc,
                               (st | j | k) != 0);
             }
             release(&empty[stage]);
@@ -465,35 +515,60 @@ __global__ void __launch_bounds__(PairCfg<BN, WIN, RF32, NORES>::THREADS, 1)
     uint8_t* st_raw = wbuf;
     uint8_t* st_act = wbuf + C::RBOX_BYTES;  // RoPE: the head's second rotation half
     constexpr int RES_OFF = C::RBOX_BYTES + C::ABOX_BYTES;  // the residual ring after the raw and act boxes
+    constexpr int NRING = C::NRES > 0 ? C::NRES : 1;         // its length (NORES: no ring, never indexed)
     uint64_t* rb = rbar + C::NRES * ew;
     const bool has_res = !NORES && (flags & EPI_RESIDUAL) != 0;  // one-segment GEMMs only
     const int a0 = p.seg[0].act, a1 = p.nseg > 1 ? p.seg[1].act : a0;
     const int res_x = p.pair_res_x, raw_x = p.pair_raw_x, act_x = p.pair_act_x;
     const uint32_t tempty_leader0 = mapa_shared(smem_u32(&tempty[0]), 0);
 
-    // residual boxes run NRES boxes ahead: box u (this warp's u-th 32-column chunk over its tiles) goes to buffer
-    // u % NRES
+    // this warp's 32-column boxes of an item, [cb, ce) counted from the item's first column: CHUNKS of a whole
+    // tile, or its column group's share of a half tile's HALF_CHUNKS (the first groups take the odd ones)
+    constexpr int GROUPS = C::EPI_WARPS / 4;
+    auto chunk_range = [&](int hf, int& cb, int& ce) {
+      if (!C::SPLIT || hf < 0) {
+        cb = h * C::CHUNKS;
+        ce = cb + C::CHUNKS;
+      } else {
+        constexpr int per = (C::HALF_CHUNKS + GROUPS - 1) / GROUPS;
+        cb = h * per;
+        ce = cb + per < C::HALF_CHUNKS ? cb + per : C::HALF_CHUNKS;
+      }
+    };
+    static_assert(!C::SPLIT || (GROUPS - 1) * ((C::HALF_CHUNKS + GROUPS - 1) / GROUPS) < C::HALF_CHUNKS,
+                  "every epilogue warp has a box of a half tile");
+
+    // residual boxes run NRES boxes ahead: box u (this warp's u-th 32-column chunk over its items; CHUNKS per whole
+    // tile, and fewer for a pair's last item if that is a half tile) goes to buffer u % NRES
     auto res_issue = [&](int u) {
-      const int i = u / C::CHUNKS, c = u - i * C::CHUNKS;
-      const int tile = pair + i * npairs;
-      if (tile >= num_tiles) return;
+      const int i = u / C::CHUNKS, k = u - i * C::CHUNKS;
+      const int it = pair + i * npairs;
+      if (it >= num_items) return;
+      int hf, cb, ce;
+      const int tile = item_tile(it, hf);
+      chunk_range(hf, cb, ce);
+      if (cb + k >= ce) return;
       const int mrow = (tile / n_tiles) * 256 + (int)rank * 128 + q * 32;
-      const int col = (tile % n_tiles) * BN + h * C::WARP_COLS + c * 32;
-      mbar_expect_tx(&rb[u % C::NRES], C::RBOX_BYTES);
-      tma_load_2d(wbuf + RES_OFF + (u % C::NRES) * C::RBOX_BYTES, &tmRes, &rb[u % C::NRES], res_x + col, mrow);
+      const int col = (tile % n_tiles) * BN + (hf > 0 ? BN / 2 : 0) + (cb + k) * 32;
+      mbar_expect_tx(&rb[u % NRING], C::RBOX_BYTES);
+      tma_load_2d(wbuf + RES_OFF + (u % NRING) * C::RBOX_BYTES, &tmRes, &rb[u % NRING], res_x + col, mrow);
     };
     if (has_res && lane == 0)
       for (int i = 0; i < C::NRES; i++) res_issue(i);
 
     int local = 0, u = 0;
     bool ok = true;
-    for (int tile = pair; tile < num_tiles && ok; tile += npairs, local++) {
+    for (int it = pair; it < num_items && ok; it += npairs, local++) {
+      int hf, cb, ce;
+      const int tile = item_tile(it, hf);
+      chunk_range(hf, cb, ce);
       const int acc = local & 1;
       const uint32_t acc_phase = (local >> 1) & 1;
       const int mrow = (tile / n_tiles) * 256 + (int)rank * 128 + q * 32;
       const int r = mrow + lane;
       const float m = r < p.g.rows ? __ldg(p.g.rowmask + r) : 0.0f;
-      const int ncol0 = (tile % n_tiles) * BN + h * C::WARP_COLS;
+      const int icol0 = (tile % n_tiles) * BN + (hf > 0 ? BN / 2 : 0);  // the item's first column
+      const int ncol0 = icol0 + h * C::WARP_COLS;                         // RoPE / SwiGLU: whole tiles
       // RoPE: this warp's 32 rows of the head's cos / sin table (board-row-indexed, 432 rows per table so that 32
       // rows from any board row stay inside it), 4 KB blocks read with coalesced 128-bit loads while the
       // accumulator is computed, into shared memory as 128-byte rows with the 128-byte swizzle, from where each
@@ -529,13 +604,13 @@ __global__ void __launch_bounds__(PairCfg<BN, WIN, RF32, NORES>::THREADS, 1)
       __syncwarp();
       tc_fence_after();
       if constexpr (MODE == MODE_SEGMENTS) {
-        const uint32_t tacc = tmem_base + acc * C::ACC_COLS + ((uint32_t)(q * 32) << 16) + h * C::WARP_COLS;
+        const uint32_t tacc = tmem_base + acc * C::ACC_COLS + ((uint32_t)(q * 32) << 16);
 #pragma unroll 1
-        for (int c = 0; c < C::CHUNKS; c++, u++) {
+        for (int cc = cb; cc < ce; cc++, u++) {
           uint32_t x[32];
-          tmem_ld32(tacc + c * 32, x);
+          tmem_ld32(tacc + cc * 32, x);
           tmem_wait_ld();
-          if (c == C::CHUNKS - 1) {
+          if (cc == ce - 1) {
             // the accumulator is in registers: hand it back to the MMA issuer before the math
             tc_fence_before();
             __syncwarp();
@@ -546,7 +621,7 @@ __global__ void __launch_bounds__(PairCfg<BN, WIN, RF32, NORES>::THREADS, 1)
           for (int i = 0; i < 32; i++) v[i] = __uint_as_float(x[i]);
           if ((f0 & EPI_BOARD_BIAS) && m != 0.0f) {
             // per-board bias (one-segment GEMMs: the stem's global-feature term), 32 columns of this row's board
-            const float* bb = p.seg[0].board_bias + (size_t)(r / 400) * p.seg[0].ld_bb + ncol0 + c * 32;
+            const float* bb = p.seg[0].board_bias + (size_t)(r / 400) * p.seg[0].ld_bb + icol0 + cc * 32;
 #pragma unroll
             for (int j = 0; j < 32; j += 4) {
               const float4 q = __ldg(reinterpret_cast<const float4*>(bb + j));
@@ -563,12 +638,12 @@ __global__ void __launch_bounds__(PairCfg<BN, WIN, RF32, NORES>::THREADS, 1)
             for (int i = 0; i < 32; i++) v[i] *= m;
           }
           if (has_res) {
-            if (!mbar_wait(&rb[u % C::NRES], (u / C::NRES) & 1, p.err, DEV_TIMEOUT_EPILOGUE)) {
+            if (!mbar_wait(&rb[u % NRING], (u / NRING) & 1, p.err, DEV_TIMEOUT_EPILOGUE)) {
               *abort_flag = 1;
               ok = false;
               break;
             }
-            const uint8_t* rbox = wbuf + RES_OFF + (u % C::NRES) * C::RBOX_BYTES;
+            const uint8_t* rbox = wbuf + RES_OFF + (u % NRING) * C::RBOX_BYTES;
             if constexpr (RF32) {
 #pragma unroll
               for (int j = 0; j < 8; j++) {
@@ -596,7 +671,7 @@ __global__ void __launch_bounds__(PairCfg<BN, WIN, RF32, NORES>::THREADS, 1)
           // the previous box's stores must have read the staging boxes before they are overwritten
           if (lane == 0) bulk_wait_read0();
           __syncwarp();
-          const int col = ncol0 + c * 32;
+          const int col = icol0 + cc * 32;
           const int cf = col < split ? f0 : f1;  // this box's segment
           if (cf & EPI_RAW) {
             float o[32];

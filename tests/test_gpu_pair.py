@@ -1,9 +1,10 @@
 """The CTA-pair GEMM (the default for one- and two-segment convolutions and token linears) against the one-CTA GEMM
 (KATAGO_CUDA_PAIR=0), the pair kernel without A windows (KATAGO_CUDA_PAIR_WIN=0), the pair kernel without the
-64-column tiles that small batches get (KATAGO_CUDA_PAIR_NARROW=0) and the float64 oracle: the trunk's tile widths
-(128, 192, 256: b10c128, small-nbt, wide-nbt; 64 at batches 1 and 5) on ragged batches whose last 256-row pair tile
-is mostly past the batch's rows, and the transformer's token linears (fused RoPE, SwiGLU, masked accumulators, the
-float32 residual stream of the bf16 tier). Tolerance: the 2-byte tiers' 2e-2 (north_star)."""
+64-column tiles that small batches get (KATAGO_CUDA_PAIR_NARROW=0), without the column-half items of a last, partly
+filled round of windowed tiles (KATAGO_CUDA_PAIR_SPLIT=0) and the float64 oracle: the trunk's tile widths (128, 192,
+256: b10c128, small-nbt, wide-nbt; 64 at batches 1 and 5) on ragged batches whose last 256-row pair tile is mostly
+past the batch's rows, and the transformer's token linears (fused RoPE, SwiGLU, masked accumulators, the float32
+residual stream of the bf16 tier). Tolerance: the 2-byte tiers' 2e-2 (north_star)."""
 
 import os
 
@@ -22,7 +23,8 @@ TOL = 2e-2
 
 def forward(name, env, spatial, glob, meta=None, prec=kc.PRECISION_F16):
     """A fresh plan built under `env` (the GEMM selection is read when the plan is built)."""
-    saved = {k: os.environ.get(k) for k in ("KATAGO_CUDA_PAIR", "KATAGO_CUDA_PAIR_WIN", "KATAGO_CUDA_PAIR_NARROW")}
+    saved = {k: os.environ.get(k) for k in ("KATAGO_CUDA_PAIR", "KATAGO_CUDA_PAIR_WIN", "KATAGO_CUDA_PAIR_NARROW",
+                                            "KATAGO_CUDA_PAIR_SPLIT")}
     try:
         for k in saved:
             os.environ.pop(k, None)
@@ -46,6 +48,8 @@ def test_pair_gemm_matches_one_cta_gemm_and_oracle(name, batch):
     runs = {"pair": forward(name, {}, spatial, glob),
             "pair without windows": forward(name, {"KATAGO_CUDA_PAIR_WIN": "0"}, spatial, glob),
             "pair, wide tiles only": forward(name, {"KATAGO_CUDA_PAIR_NARROW": "0"}, spatial, glob),
+            "pair, whole tiles only": forward(name, {"KATAGO_CUDA_PAIR_NARROW": "0", "KATAGO_CUDA_PAIR_SPLIT": "0"},
+                                              spatial, glob),
             "one-CTA": forward(name, {"KATAGO_CUDA_PAIR": "0"}, spatial, glob)}
     for label, got in runs.items():
         for k in KEYS:
