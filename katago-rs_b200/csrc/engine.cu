@@ -892,6 +892,44 @@ struct Builder {
                                                     Ip->scale1, Ip->scale2, value_mode ? 1 : 0, out);
     });
   }
+  // The gpool block's pooling, bias matmul and biased batch-norm + activation as one launch per board
+  // (gpool_mid_kernel), bit-identical to the three launches it replaces; false where its shapes do not fit (the
+  // caller then emits pool, fc and bias_bnact). KATAGO_CUDA_GPOOL_FUSED=0: always the three launches.
+  bool gpool_mid(Tensor G, int gc, Tensor REG, int rc, const MatMulDesc& mm, const BNDesc& bn, Act act, Tensor y) {
+    const char* e = std::getenv("KATAGO_CUDA_GPOOL_FUSED");
+    if (e && e[0] == '0') return false;
+    if (gc % 8 || rc % 8 || G.ld % 8 || REG.ld % 8 || y.ld % 8 || mm.ic != 3 * gc || mm.oc != rc ||
+        (gc + 7) / 8 > POOL_THREADS)
+      return false;
+    const int smem = (pool_red_floats(gc) + 3 * gc + 9 * rc) * (int)sizeof(float);
+    if (smem > 227 * 1024) return false;
+    if (pass == 0) return true;
+    const float* w = up(mm.w);
+    const float* sc = up(bn.merged_scale);
+    const float* sh = up(bn.merged_bias);
+    const int cw = std::min(y.ld, round_up(rc, 64));
+    auto kernel_for = [](Act a) {
+      switch (a) {
+        case 1: return gpool_mid_kernel<T, 1>;
+        case 2: return gpool_mid_kernel<T, 2>;
+        case 3: return gpool_mid_kernel<T, 3>;
+        default: return gpool_mid_kernel<T, 0>;
+      }
+    };
+    auto kernel = kernel_for(act);
+    if (smem > 48 * 1024) allow_smem(kernel, smem);
+    Engine::Impl* Ip = &I;
+    add(CLS_OTHER, [=](cudaStream_t st, int n) {
+      GpoolMidParams q;
+      q.g = G.p, q.ld_g = G.ld, q.gc = gc;
+      q.reg = REG.p, q.ld_reg = REG.ld, q.rc = rc;
+      q.w = w, q.scale = sc, q.shift = sh;
+      q.rowmask = Ip->rowmask, q.mask_sum = Ip->mask_sum, q.scale1 = Ip->scale1, q.scale2 = Ip->scale2;
+      q.y = y.p, q.ld_y = y.ld, q.cw = cw;
+      launch_pdl(kernel, dim3(n), dim3(POOL_THREADS), smem, st, q);
+    });
+    return true;
+  }
   void fc(const float* in, int in_ld, const MatMulDesc& mm, const MatBiasDesc* mb, Act act, float* out, int out_ld,
           int out_off, int out_stride) {
     const float* w = up(mm.w);
@@ -966,11 +1004,13 @@ struct Builder {
       s0.raw = REG;
       gemm(conv_spec(CLS_CONV3, XA, C, {&b.regular, &b.gpool_conv},
                      {s0, act_seg(w16(gc), b.gpool_bn, b.gpool_act, G)}));
-      float* pooled = fbuffer(F_POOL, 3 * gc);
-      float* gbias = fbuffer(F_GBIAS, rc);
-      pool(G, 0, gc, false, pooled);
-      fc(pooled, 3 * gc, b.gpool_to_bias, nullptr, ACT_IDENTITY, gbias, rc, 0, 1);
-      bias_bnact(REG, 0, gbias, b.mid_bn, b.mid_act, rc, T1);
+      if (!gpool_mid(G, gc, REG, rc, b.gpool_to_bias, b.mid_bn, b.mid_act, T1)) {
+        float* pooled = fbuffer(F_POOL, 3 * gc);
+        float* gbias = fbuffer(F_GBIAS, rc);
+        pool(G, 0, gc, false, pooled);
+        fc(pooled, 3 * gc, b.gpool_to_bias, nullptr, ACT_IDENTITY, gbias, rc, 0, 1);
+        bias_bnact(REG, 0, gbias, b.mid_bn, b.mid_act, rc, T1);
+      }
       gemm(conv_spec(CLS_CONV3, T1, rc, {&b.final_conv}, {close_seg(w16(C), X, XA, next, false, raw_live)}));
     } else if (b.kind == BLOCK_NESTED) {
       // bin2onnx.py nested_bottleneck_block :1263-1269

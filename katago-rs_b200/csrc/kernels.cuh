@@ -238,21 +238,21 @@ static __global__ void board_kernel(const __grid_constant__ BoardParams p) {
 // (the channels up to the next multiple of 8 are read and dropped).
 // ---------------------------------------------------------------------------------------------------------------
 constexpr int POOL_THREADS = 512;
+// Shared memory of one board's pooling: [RL][Cp] sums, then [RL][Cp] maxima.
+__host__ __device__ constexpr int pool_red_floats(int C) {
+  return 2 * (POOL_THREADS / ((C + 7) / 8)) * ((C + 7) / 8) * 8;
+}
+// Board b's pooled [3C] into o, by a block of POOL_THREADS threads (red: pool_red_floats(C) floats of shared memory;
+// o may be shared or global memory). Ends with the block synchronised when o is shared.
 template <typename T>
-__global__ void __launch_bounds__(POOL_THREADS) pool_kernel(const T* __restrict__ x, int ld, int c0, int C,
-                                                            const float* __restrict__ rowmask,
-                                                            const float* __restrict__ mask_sum,
-                                                            const float* __restrict__ scale1,
-                                                            const float* __restrict__ scale2, int value_mode,
-                                                            float* __restrict__ out) {
-  pdl_wait();
-  pdl_trigger();
-  extern __shared__ float pool_red[];  // [RL][Cp] sums, then [RL][Cp] maxima
-  const int b = blockIdx.x;
+__device__ __forceinline__ void pool_board(const T* __restrict__ x, int ld, int c0, int C, const float* __restrict__ rowmask,
+                                           const float* __restrict__ mask_sum, const float* __restrict__ scale1,
+                                           const float* __restrict__ scale2, int value_mode, int b, float* red,
+                                           float* o) {
   const int CG = (C + 7) >> 3, Cp = CG * 8, RL = POOL_THREADS / CG;
   const int g = threadIdx.x % CG, rl = threadIdx.x / CG;
-  float* ssum = pool_red;
-  float* smax = pool_red + RL * Cp;
+  float* ssum = red;
+  float* smax = red + RL * Cp;
   if (rl < RL) {
     float s[8], mx[8];
 #pragma unroll
@@ -287,11 +287,25 @@ __global__ void __launch_bounds__(POOL_THREADS) pool_kernel(const T* __restrict_
       mx = fmaxf(mx, smax[i * Cp + c]);
     }
     const float mean = s / mask_sum[b];
-    float* o = out + (size_t)b * 3 * C;
     o[c] = mean;
     o[C + c] = mean * scale1[b];
     o[2 * C + c] = value_mode ? mean * scale2[b] : mx;
   }
+  __syncthreads();
+}
+
+template <typename T>
+__global__ void __launch_bounds__(POOL_THREADS) pool_kernel(const T* __restrict__ x, int ld, int c0, int C,
+                                                            const float* __restrict__ rowmask,
+                                                            const float* __restrict__ mask_sum,
+                                                            const float* __restrict__ scale1,
+                                                            const float* __restrict__ scale2, int value_mode,
+                                                            float* __restrict__ out) {
+  pdl_wait();
+  pdl_trigger();
+  extern __shared__ float pool_red[];
+  const int b = blockIdx.x;
+  pool_board<T>(x, ld, c0, C, rowmask, mask_sum, scale1, scale2, value_mode, b, pool_red, out + (size_t)b * 3 * C);
 }
 
 // ---------------------------------------------------------------------------------------------------------------
@@ -357,24 +371,15 @@ __global__ void __launch_bounds__(FC_THREADS) fc_kernel(const float* __restrict_
 // ---------------------------------------------------------------------------------------------------------------
 // One thread per 8 channels of a row (16-byte loads and stores); the activation fixed at compile time. x's and y's
 // row pitches and xc0 are multiples of 8 elements, Cw a multiple of 8.
+// Channels [c, c + 8) of row r with mask m; bb: the row's board bias (or null).
 template <typename TI, typename T, int ACT>
-__global__ void bias_bnact_kernel(const TI* __restrict__ x, int xld, int xc0, const float* __restrict__ board_bias,
-                                  const float* __restrict__ scale, const float* __restrict__ bias,
-                                  const float* __restrict__ rowmask, int rows, int C, int Cw, T* __restrict__ y,
-                                  int yld) {
-  pdl_wait();
-  pdl_trigger();
-  const int per_row = Cw >> 3;
-  const int idx = blockIdx.x * blockDim.x + threadIdx.x;
-  if (idx >= rows * per_row) return;
-  const int r = idx / per_row;
-  const int c = (idx - r * per_row) << 3;
-  const float m = __ldg(rowmask + r);
+__device__ __forceinline__ void bias_bnact_vec(const TI* __restrict__ x, int xld, int xc0, const float* bb,
+                                               const float* __restrict__ scale, const float* __restrict__ bias,
+                                               float m, int r, int c, int C, T* __restrict__ y, int yld) {
   float o[8];
   if (c < C && m != 0.0f) {
     float v[8];
     load_vec<TI, 8>(x + (size_t)r * xld + xc0 + c, v);
-    const float* bb = board_bias ? board_bias + (size_t)(r / 400) * C : nullptr;
     if (c + 8 <= C && (C & 3) == 0) {
       // whole vector inside the channels: parameters as 16-byte loads
       float sc[8], bi[8], bv[8];
@@ -395,7 +400,7 @@ __global__ void bias_bnact_kernel(const TI* __restrict__ x, int xld, int xc0, co
         const int cc = c + i;
         if (cc < C) {
           float t = v[i];
-          if (bb) t = t + __ldg(bb + cc);
+          if (bb) t = t + bb[cc];
           t = t * __ldg(scale + cc);
           t = t + __ldg(bias + cc);
           o[i] = act_fn<ACT>(t) * m;
@@ -409,6 +414,84 @@ __global__ void bias_bnact_kernel(const TI* __restrict__ x, int xld, int xc0, co
     for (int i = 0; i < 8; i++) o[i] = 0.0f;
   }
   store_vec<T, 8>(y + (size_t)r * yld + c, o);
+}
+
+template <typename TI, typename T, int ACT>
+__global__ void bias_bnact_kernel(const TI* __restrict__ x, int xld, int xc0, const float* __restrict__ board_bias,
+                                  const float* __restrict__ scale, const float* __restrict__ bias,
+                                  const float* __restrict__ rowmask, int rows, int C, int Cw, T* __restrict__ y,
+                                  int yld) {
+  pdl_wait();
+  pdl_trigger();
+  const int per_row = Cw >> 3;
+  const int idx = blockIdx.x * blockDim.x + threadIdx.x;
+  if (idx >= rows * per_row) return;
+  const int r = idx / per_row;
+  const int c = (idx - r * per_row) << 3;
+  const float* bb = board_bias ? board_bias + (size_t)(r / 400) * C : nullptr;
+  bias_bnact_vec<TI, T, ACT>(x, xld, xc0, bb, scale, bias, __ldg(rowmask + r), r, c, C, y, yld);
+}
+
+// ---------------------------------------------------------------------------------------------------------------
+// The gpool block's middle in one launch (bin2onnx.py gpool_block :1250-1261 after the two convolutions): per board
+// (one block of POOL_THREADS), pool the gpool branch G (pool_board), the pooled vector times gpool_to_bias
+// ([3 gc][rc], fc_kernel's arithmetic: eight input slices summed in order) into the regular branch's bias, then
+// T1 = act((REG + bias) * scale + shift) * mask over the board's 400 rows (bias_bnact_vec). Shared memory:
+// pool_red_floats(gc) + 3 gc + 8 rc + rc floats.
+// ---------------------------------------------------------------------------------------------------------------
+struct GpoolMidParams {
+  const void* g;     // gpool branch [rows][ld_g], channels [0, gc)
+  int ld_g, gc;
+  const void* reg;   // regular branch [rows][ld_reg], channels [0, rc)
+  int ld_reg, rc;
+  const float* w;    // [3 gc][rc]
+  const float* scale;
+  const float* shift;
+  const float* rowmask;
+  const float* mask_sum;
+  const float* scale1;
+  const float* scale2;
+  void* y;           // T1 [rows][ld_y], channels [0, cw) written (zero from rc on)
+  int ld_y, cw;
+};
+
+template <typename T, int ACT>
+__global__ void __launch_bounds__(POOL_THREADS) gpool_mid_kernel(const __grid_constant__ GpoolMidParams p) {
+  pdl_wait();
+  pdl_trigger();
+  extern __shared__ float gm_smem[];
+  float* red = gm_smem;
+  float* pooled = red + pool_red_floats(p.gc);
+  float* part = pooled + 3 * p.gc;  // [8][rc]
+  float* gb = part + 8 * p.rc;
+  const int b = blockIdx.x;
+  pool_board<T>(static_cast<const T*>(p.g), p.ld_g, 0, p.gc, p.rowmask, p.mask_sum, p.scale1, p.scale2, 0, b, red,
+                pooled);
+  const int ic = 3 * p.gc;
+  constexpr int NS = 8;  // input slices, as fc_kernel's eight warps
+  for (int q = threadIdx.x; q < NS * p.rc; q += POOL_THREADS) {
+    const int sl = q / p.rc, o = q - sl * p.rc;
+    const int i0 = (int)((long long)ic * sl / NS), i1 = (int)((long long)ic * (sl + 1) / NS);
+    float a = 0.0f;
+    for (int i = i0; i < i1; i++) a += pooled[i] * __ldg(p.w + (size_t)i * p.rc + o);
+    part[sl * p.rc + o] = a;
+  }
+  __syncthreads();
+  for (int o = threadIdx.x; o < p.rc; o += POOL_THREADS) {
+    float v = 0.0f;
+#pragma unroll
+    for (int j = 0; j < NS; j++) v += part[j * p.rc + o];
+    gb[o] = v;
+  }
+  __syncthreads();
+  const int per_row = p.cw >> 3;
+  for (int idx = threadIdx.x; idx < 400 * per_row; idx += POOL_THREADS) {
+    const int rr = idx / per_row;
+    const int r = b * 400 + rr;
+    const int c = (idx - rr * per_row) << 3;
+    bias_bnact_vec<T, T, ACT>(static_cast<const T*>(p.reg), p.ld_reg, 0, gb, p.scale, p.shift, __ldg(p.rowmask + r),
+                              r, c, p.rc, static_cast<T*>(p.y), p.ld_y);
+  }
 }
 
 // ---------------------------------------------------------------------------------------------------------------

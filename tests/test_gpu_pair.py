@@ -1,7 +1,7 @@
 """The CTA-pair GEMM (the default for one- and two-segment convolutions and token linears) against the one-CTA GEMM
 (KATAGO_CUDA_PAIR=0), the pair kernel without A windows (KATAGO_CUDA_PAIR_WIN=0), the pair kernel without the
 64-column tiles that small batches get (KATAGO_CUDA_PAIR_NARROW=0), without the column-half items of a last, partly
-filled round of windowed tiles (KATAGO_CUDA_PAIR_SPLIT=0) and the float64 oracle: the trunk's tile widths (128, 192,
+filled round of tiles (KATAGO_CUDA_PAIR_SPLIT=0) and the float64 oracle: the trunk's tile widths (128, 192,
 256: b10c128, small-nbt, wide-nbt; 64 at batches 1 and 5) on ragged batches whose last 256-row pair tile is mostly
 past the batch's rows, and the transformer's token linears (fused RoPE, SwiGLU, masked accumulators, the float32
 residual stream of the bf16 tier). Tolerance: the 2-byte tiers' 2e-2 (north_star)."""
@@ -24,7 +24,7 @@ TOL = 2e-2
 def forward(name, env, spatial, glob, meta=None, prec=kc.PRECISION_F16):
     """A fresh plan built under `env` (the GEMM selection is read when the plan is built)."""
     saved = {k: os.environ.get(k) for k in ("KATAGO_CUDA_PAIR", "KATAGO_CUDA_PAIR_WIN", "KATAGO_CUDA_PAIR_NARROW",
-                                            "KATAGO_CUDA_PAIR_SPLIT")}
+                                            "KATAGO_CUDA_PAIR_SPLIT", "KATAGO_CUDA_GPOOL_FUSED")}
     try:
         for k in saved:
             os.environ.pop(k, None)
@@ -82,3 +82,14 @@ def test_pair_token_linears(name, prec):
     if prec == kc.PRECISION_F16:
         diff = {k: float(np.abs(runs["pair"][k] - runs["one-CTA"][k]).max()) for k in KEYS}
         assert max(diff.values()) <= TOL, diff
+
+
+@pytest.mark.parametrize("prec", [kc.PRECISION_F16, kc.PRECISION_F32])
+def test_gpool_mid_fused_is_bit_identical(prec):
+    """The gpool block's pooling, bias matmul and biased batch norm as one launch per board give the outputs of the
+    three launches they replace, bit for bit (small-nbt: two gpool blocks of 128 + 64 channels; mixed boards)."""
+    spatial, glob, _, _ = inputs.synthetic_inputs(7, 4242, (9, 13, 19), rich=True)
+    fused = forward("small-nbt", {}, spatial, glob, prec=prec)
+    three = forward("small-nbt", {"KATAGO_CUDA_GPOOL_FUSED": "0"}, spatial, glob, prec=prec)
+    for k in KEYS:
+        np.testing.assert_array_equal(fused[k], three[k])
