@@ -11,12 +11,13 @@
 //   S = Q K^T (M = 128, N = 2 x 208, K = 64) into TMEM [0, 416);
 //   row max over S (exchanged in shared memory), p = 2^((s - max) * scale * log2 e) for on-board keys (0 for
 //   off-board, halo and out-of-board keys: an additive -inf key bias), P (bf16 / f16) into shared memory in the
-//   K-major 128B-swizzled layout of an MMA A operand, keys 0..255 then, once the MMAs have read those, keys
-//   256..447 (keys 416..447 zero);
-//   O = P V (M = 128, N = 64, K = 448, V as an MN-major B operand) into TMEM [416, 480) in those two halves, then
-//   O divided by the row sum.
+//   K-major 128B-swizzled layout of an MMA A operand, in five 64-key buffers: the first pass keys 0..191 (buffers
+//   0..2); the second pass first keys 192..255 (buffer 3) and 384..447 (buffer 4; keys 416..447 zero), which the
+//   first pass's MMAs do not read, then, once they have read buffers 0 and 1, keys 256..383 there;
+//   O = P V (M = 128, N = 64, K = 448, V as an MN-major B operand) into TMEM [416, 480) after each pass, the
+//   K-blocks in key order, then O divided by the row sum.
 // There are no producer or MMA warps: one elected thread of warp 0 issues the TMA loads and the MMAs at the points
-// where its warp waits for all warps anyway (after each half of P), so the CTA is 512 threads with 128 registers
+// where its warp waits for all warps anyway (after each pass), so the CTA is 512 threads with 128 registers
 // each. The next tile's S is computed while the warps write the current tile's output.
 // Off-board keys get weight exactly 0 here; in the reference their weight exp(-3e4 + ...) underflows to 0 too.
 #pragma once
@@ -46,9 +47,9 @@ struct AttnCfg {
   static constexpr int V_BYTES = PKEYS * 128;          // 57344
   static constexpr int Q_OFF = V_OFF + V_BYTES;        // 110592
   static constexpr int Q_BYTES = 128 * 128;            // 16384
-  static constexpr int P_OFF = Q_OFF + Q_BYTES;        // 126976: half of P, 4 tiles of 128 queries x 64 keys
-  static constexpr int P_BYTES = 4 * 128 * 128;        // 65536
-  static constexpr int BIAS_OFF = P_OFF + P_BYTES;     // 192512: key bias, 0 or -inf
+  static constexpr int P_OFF = Q_OFF + Q_BYTES;        // 126976: P buffers 0..4, tiles of 128 queries x 64 keys
+  static constexpr int P_BYTES = 5 * 128 * 128;        // 81920
+  static constexpr int BIAS_OFF = P_OFF + P_BYTES;     // 208896: key bias, 0 or -inf
   static constexpr int WARPS = 16;                     // 4 per TMEM lane quarter, one per key quarter
   static constexpr int RED_OFF = BIAS_OFF + KEYS * 4;  // row max and row sum of each key quarter: [2][4][128]
   static constexpr int BAR_OFF = RED_OFF + 2 * 4 * 128 * 4;
@@ -235,27 +236,27 @@ __global__ void __launch_bounds__(AttnCfg::THREADS, 1)
     if (m == -INFINITY) m = 0.0f;  // no on-board key: every p is 0
     const float msl = m * sl;
     float sum = 0.0f;
-    // keys 0..255: this warp's 64 keys -> P tile kq
+    // first pass, keys 0..191: this warp's 48 keys -> P buffers 0..2
     if (ok && live) {
-      uint32_t x[32], y[32];
-      tmem_ld32(trow + kq * 64, x);
-      tmem_ld32(trow + kq * 64 + 32, y);
+      uint32_t x[32], y[16];
+      tmem_ld32(trow + kq * 48, x);
+      tmem_ld16(trow + kq * 48 + 32, y);
       tmem_wait_ld();
-      attn_exp_group<T, 32>(x, kbias + kq * 64, sl, msl, sum, P, r, kq * 64);
-      attn_exp_group<T, 32>(y, kbias + kq * 64 + 32, sl, msl, sum, P, r, kq * 64 + 32);
+      attn_exp_group<T, 32>(x, kbias + kq * 48, sl, msl, sum, P, r, kq * 48);
+      attn_exp_group<T, 16>(y, kbias + kq * 48 + 32, sl, msl, sum, P, r, kq * 48 + 32);
     }
     fence_proxy_async_smem();
     tc_fence_before();
     __syncwarp();
     if (lane == 0) mbar_arrive(pa_full);
     if (ctl) {
-      // O = P[keys 0..255] V once every warp wrote its part and the previous tile's O was read; then the next
+      // O = P[keys 0..191] V once every warp wrote its part and the previous tile's O was read; then the next
       // query tile into the Q buffer (S_t has completed: its commit was observed above)
       cok = cok && mbar_wait(pa_full, ph, p.err, DEV_TIMEOUT_MMA) &&
             (t == 0 || mbar_wait(o_empty, (t - 1) & 1, p.err, DEV_TIMEOUT_MMA));
       if (cok) {
         tc_fence_after();
-        for (int kb = 0; kb < 4; kb++)
+        for (int kb = 0; kb < 3; kb++)
 #pragma unroll
           for (int k = 0; k < 4; k++)
             umma_f16(tmem + C::O_COL, make_sw128_desc(sp + kb * 16384 + k * 32),
@@ -267,39 +268,46 @@ __global__ void __launch_bounds__(AttnCfg::THREADS, 1)
         }
       }
     }
-    // keys 256..415, once the MMAs have read the first half: this warp's 40 keys (kq 3: also the zero keys 416..447)
+    // second pass, into the buffers the first pass's MMAs do not read: this warp's 16 of keys 192..255 (buffer 3)
+    // and 8 of keys 384..415 (buffer 4), and 8 of buffer 4's zero keys 416..447 (V rows there are finite: the next
+    // board or TMA's zero fill)
+    uint8_t* P4 = P + 4 * 16384;
+    if (ok && live) {
+      uint32_t x[16], z[8];
+      tmem_ld16(trow + 192 + kq * 16, x);
+      tmem_ld8(trow + 384 + kq * 8, z);
+      tmem_wait_ld();
+      attn_exp_group<T, 16>(x, kbias + 192 + kq * 16, sl, msl, sum, P, r, 192 + kq * 16);
+      attn_exp_group<T, 8>(z, kbias + 384 + kq * 8, sl, msl, sum, P4, r, kq * 8);
+      *reinterpret_cast<uint4*>(P4 + r * 128 + (((4 + kq) ^ (r & 7)) * 16)) = make_uint4(0, 0, 0, 0);
+    }
+    // then, once the first pass's MMAs have read buffers 0 and 1: this warp's 32 of keys 256..383 there
     ok = ok && mbar_wait(pa_free, ph, p.err, DEV_TIMEOUT_EPILOGUE);
     __syncwarp();
     tc_fence_after();
     if (ok && live) {
-      const int c0 = 256 + kq * 40;
-      uint32_t x[32], z[8];
-      tmem_ld32(trow + c0, x);
-      tmem_ld8(trow + c0 + 32, z);
+      uint32_t x[32];
+      tmem_ld32(trow + 256 + kq * 32, x);
       tmem_wait_ld();
-      attn_exp_group<T, 32>(x, kbias + c0, sl, msl, sum, P, r, c0 - 256);
-      attn_exp_group<T, 8>(z, kbias + c0 + 32, sl, msl, sum, P, r, c0 + 32 - 256);
-      if (kq == 3) {
-        // keys 416..447: P zero (V rows there are finite: the next board or TMA's zero fill)
-        uint8_t* tile = P + 2 * 16384 + r * 128;
-#pragma unroll
-        for (int j = 4; j < 8; j++) *reinterpret_cast<uint4*>(tile + ((j ^ (r & 7)) * 16)) = make_uint4(0, 0, 0, 0);
-      }
+      attn_exp_group<T, 32>(x, kbias + 256 + kq * 32, sl, msl, sum, P, r, kq * 32);
     }
     fence_proxy_async_smem();
     tc_fence_before();
     __syncwarp();
     if (lane == 0) mbar_arrive(pb_full);
     if (ctl) {
-      // O += P[keys 256..447] V (the same buffer, refilled); then the next tile's S (every warp has read S_t)
+      // O += P[keys 192..447] V, K-blocks 3..6 from buffers 3, 0, 1, 4; then the next tile's S (every warp has
+      // read S_t)
       cok = cok && mbar_wait(pb_full, ph, p.err, DEV_TIMEOUT_MMA);
       if (cok) {
         tc_fence_after();
-        for (int kb = 4; kb < 7; kb++)
+        for (int kb = 3; kb < 7; kb++) {
+          const int buf = kb == 3 ? 3 : kb == 6 ? 4 : kb - 4;
 #pragma unroll
           for (int k = 0; k < 4; k++)
-            umma_f16(tmem + C::O_COL, make_sw128_desc(sp + (kb - 4) * 16384 + k * 32),
+            umma_f16(tmem + C::O_COL, make_sw128_desc(sp + buf * 16384 + k * 32),
                      make_sw128_mn_desc(sv + (kb * 64 + k * 16) * 128), IDESC_O, 1);
+        }
         umma_commit(o_full);
         if (t + 1 < C::QTILES) issue_s(t + 1);
       }
