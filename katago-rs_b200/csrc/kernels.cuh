@@ -437,7 +437,10 @@ __global__ void bias_bnact_kernel(const TI* __restrict__ x, int xld, int xc0, co
 // (one block of POOL_THREADS), pool the gpool branch G (pool_board), the pooled vector times gpool_to_bias
 // ([3 gc][rc], fc_kernel's arithmetic: eight input slices summed in order) into the regular branch's bias, then
 // T1 = act((REG + bias) * scale + shift) * mask over the board's 400 rows (bias_bnact_vec). Shared memory:
-// pool_red_floats(gc) + 3 gc + 8 rc + rc floats.
+// pool_red_floats(gc) + 3 gc + 8 rc + rc floats. With gridDim.y = S > 1 (small batches, where one block per board
+// leaves most SMs idle) block (b, s) pools the whole board but computes only its column group's bias entries and
+// output vectors: vectors [cw/8 * s / S, cw/8 * (s + 1) / S) of each row. Every output value takes the same
+// arithmetic in the same order whatever S is.
 // ---------------------------------------------------------------------------------------------------------------
 struct GpoolMidParams {
   const void* g;     // gpool branch [rows][ld_g], channels [0, gc)
@@ -467,28 +470,32 @@ __global__ void __launch_bounds__(POOL_THREADS) gpool_mid_kernel(const __grid_co
   const int b = blockIdx.x;
   pool_board<T>(static_cast<const T*>(p.g), p.ld_g, 0, p.gc, p.rowmask, p.mask_sum, p.scale1, p.scale2, 0, b, red,
                 pooled);
+  // this block's output vectors [v0, v1) of each row and bias columns [o0, o1)
+  const int per_row = p.cw >> 3;
+  const int v0 = per_row * (int)blockIdx.y / (int)gridDim.y, v1 = per_row * ((int)blockIdx.y + 1) / (int)gridDim.y;
+  const int o0 = v0 * 8, o1 = v1 * 8 < p.rc ? v1 * 8 : p.rc, ncol = o1 - o0;
   const int ic = 3 * p.gc;
   constexpr int NS = 8;  // input slices, as fc_kernel's eight warps
-  for (int q = threadIdx.x; q < NS * p.rc; q += POOL_THREADS) {
-    const int sl = q / p.rc, o = q - sl * p.rc;
+  for (int q = threadIdx.x; q < NS * ncol; q += POOL_THREADS) {
+    const int sl = q / ncol, o = o0 + q - sl * ncol;
     const int i0 = (int)((long long)ic * sl / NS), i1 = (int)((long long)ic * (sl + 1) / NS);
     float a = 0.0f;
     for (int i = i0; i < i1; i++) a += pooled[i] * __ldg(p.w + (size_t)i * p.rc + o);
     part[sl * p.rc + o] = a;
   }
   __syncthreads();
-  for (int o = threadIdx.x; o < p.rc; o += POOL_THREADS) {
+  for (int o = o0 + (int)threadIdx.x; o < o1; o += POOL_THREADS) {
     float v = 0.0f;
 #pragma unroll
     for (int j = 0; j < NS; j++) v += part[j * p.rc + o];
     gb[o] = v;
   }
   __syncthreads();
-  const int per_row = p.cw >> 3;
-  for (int idx = threadIdx.x; idx < 400 * per_row; idx += POOL_THREADS) {
-    const int rr = idx / per_row;
+  const int nv = v1 - v0;
+  for (int idx = threadIdx.x; idx < 400 * nv; idx += POOL_THREADS) {
+    const int rr = idx / nv;
     const int r = b * 400 + rr;
-    const int c = (idx - rr * per_row) << 3;
+    const int c = (v0 + idx - rr * nv) << 3;
     bias_bnact_vec<T, T, ACT>(static_cast<const T*>(p.reg), p.ld_reg, 0, gb, p.scale, p.shift, __ldg(p.rowmask + r),
                               r, c, p.rc, static_cast<T*>(p.y), p.ld_y);
   }

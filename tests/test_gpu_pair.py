@@ -24,7 +24,8 @@ TOL = 2e-2
 def forward(name, env, spatial, glob, meta=None, prec=kc.PRECISION_F16):
     """A fresh plan built under `env` (the GEMM selection is read when the plan is built)."""
     saved = {k: os.environ.get(k) for k in ("KATAGO_CUDA_PAIR", "KATAGO_CUDA_PAIR_WIN", "KATAGO_CUDA_PAIR_NARROW",
-                                            "KATAGO_CUDA_PAIR_SPLIT", "KATAGO_CUDA_GPOOL_FUSED")}
+                                            "KATAGO_CUDA_PAIR_SPLIT", "KATAGO_CUDA_GPOOL_FUSED",
+                                            "KATAGO_CUDA_GPOOL_GROUPS")}
     try:
         for k in saved:
             os.environ.pop(k, None)
@@ -86,10 +87,13 @@ def test_pair_token_linears(name, prec):
 
 @pytest.mark.parametrize("prec", [kc.PRECISION_F16, kc.PRECISION_F32])
 def test_gpool_mid_fused_is_bit_identical(prec):
-    """The gpool block's pooling, bias matmul and biased batch norm as one launch per board give the outputs of the
-    three launches they replace, bit for bit (small-nbt: two gpool blocks of 128 + 64 channels; mixed boards)."""
+    """The gpool block's pooling, bias matmul and biased batch norm as one launch give the outputs of the three
+    launches they replace, bit for bit (small-nbt: two gpool blocks of 128 + 64 channels; mixed boards), whether a
+    board's columns go to one block or are shared out over several (the default at this batch: 16 groups of one
+    16-byte vector per row; 3 groups: uneven)."""
     spatial, glob, _, _ = inputs.synthetic_inputs(7, 4242, (9, 13, 19), rich=True)
-    fused = forward("small-nbt", {}, spatial, glob, prec=prec)
     three = forward("small-nbt", {"KATAGO_CUDA_GPOOL_FUSED": "0"}, spatial, glob, prec=prec)
-    for k in KEYS:
-        np.testing.assert_array_equal(fused[k], three[k])
+    for env in ({}, {"KATAGO_CUDA_GPOOL_GROUPS": "1"}, {"KATAGO_CUDA_GPOOL_GROUPS": "3"}):
+        fused = forward("small-nbt", env, spatial, glob, prec=prec)
+        for k in KEYS:
+            np.testing.assert_array_equal(fused[k], three[k], err_msg=str(env))
