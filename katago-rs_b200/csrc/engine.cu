@@ -20,6 +20,7 @@
 
 #include "common.h"
 #include "attention.cuh"
+#include "gemm_chain.cuh"
 #include "gemm_pair.cuh"
 #include "kernels.cuh"
 
@@ -204,6 +205,43 @@ int launch_pair_bn(bool prepare, int pairs, cudaStream_t s, const PairMaps& m, c
   cfg.numAttrs = pdl_enabled() ? 2 : 1;
   cfg.gridDim = dim3(2 * pairs);
   KC_CUDA(cudaLaunchKernelEx(&cfg, kernel, m.a, m.b, m.res, m.raw, m.act, p));
+  return pairs;
+}
+
+// The chained closing / opening 1x1 kernel of two consecutive nested blocks (gemm_chain.cuh), launched as clusters
+// of two CTAs like the pair GEMM; `prepare` returns how many pairs fit on the device at once.
+struct ChainMaps {
+  CUtensorMap x, w1, w2, trunk, raw2, act2;
+};
+
+template <typename T>
+int launch_chain(bool prepare, int pairs, cudaStream_t s, const ChainMaps& m, const ChainParams& p) {
+  using C = ChainCfg;
+  auto kernel = gemm_chain_kernel<T>;
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute at[2];
+  at[0].id = cudaLaunchAttributeClusterDimension;
+  at[0].val.clusterDim.x = 2;
+  at[0].val.clusterDim.y = 1;
+  at[0].val.clusterDim.z = 1;
+  cfg.blockDim = dim3(C::THREADS);
+  cfg.dynamicSmemBytes = C::SMEM;
+  cfg.stream = s;
+  cfg.attrs = at;
+  cfg.numAttrs = 1;
+  if (prepare) {
+    allow_smem(kernel, C::SMEM);
+    cfg.gridDim = dim3(2);
+    int clusters = 0;
+    KC_CUDA(cudaOccupancyMaxActiveClusters(&clusters, kernel, &cfg));
+    if (clusters <= 0) fail(KC_ERR_CUDA, "CUDA backend: no CTA pair of the chained 1x1 kernel fits on this device");
+    return clusters;
+  }
+  at[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  at[1].val.programmaticStreamSerializationAllowed = 1;
+  cfg.numAttrs = pdl_enabled() ? 2 : 1;
+  cfg.gridDim = dim3(2 * pairs);
+  KC_CUDA(cudaLaunchKernelEx(&cfg, kernel, m.x, m.w1, m.w2, m.trunk, m.raw2, m.act2, p));
   return pairs;
 }
 
@@ -989,11 +1027,76 @@ struct Builder {
   // ---- blocks ----
   // raw_live: whether the stack's residual stream is read after its last block
   void emit_stack(const std::vector<BlockDesc>& v, int depth, int C, BnAct after, bool raw_live = true) {
+    bool pre_done = false;
     for (size_t i = 0; i < v.size(); i++)
-      emit_block(v[i], depth, C, consumer_bn(v, i + 1, after), i + 1 < v.size() || raw_live);
+      pre_done = emit_block(v[i], depth, C, consumer_bn(v, i + 1, after), i + 1 < v.size() || raw_live, pre_done,
+                            i + 1 < v.size() ? &v[i + 1] : nullptr);
   }
 
-  void emit_block(const BlockDesc& b, int depth, int C, BnAct next, bool raw_live = true) {
+  // A nested block's closing 1x1 and the next nested block's opening 1x1 as one launch (gemm_chain_kernel): the
+  // trunk's batch norm + activation for the opening (XA) stays in tensor memory instead of a 384-channel HBM write
+  // and read per boundary. Taken for the 2-byte tiers' 384-channel trunks with 192-channel bottlenecks (the
+  // b18c384nbt shape); KATAGO_CUDA_CHAIN=0: two launches. Returns whether it emitted the launch.
+  bool chain_boundary(const BlockDesc& b, const BlockDesc& nb, int depth, int C, BnAct next, Tensor X, Tensor MA) {
+    if constexpr (sizeof(T) != 2) {
+      return false;
+    } else {
+      const char* e = std::getenv("KATAGO_CUDA_CHAIN");
+      if (pass == 0 || !tc || (e && e[0] == '0')) return false;
+      using CC = ChainCfg;
+      const ConvDesc &c1 = b.post_conv, &c2 = nb.pre_conv;
+      if (nb.kind != BLOCK_NESTED || C != CC::N1 || c1.ky != 1 || c1.kx != 1 || c2.ky != 1 || c2.kx != 1 ||
+          c1.ic != CC::K1 || c1.oc != CC::N1 || c2.ic != CC::K2 || c2.oc != CC::N2)
+        return false;
+      const BnAct first = consumer_bn(nb.inner, 0, {&nb.post_bn, nb.post_act});
+      if (!next.bn || !first.bn) return false;
+      Tensor M2 = tensor(R_LEVEL0 + 2 * (depth + 1), c2.oc);
+      Tensor MA2 = tensor(R_LEVEL0 + 2 * (depth + 1) + 1, c2.oc);
+      if (X.f32 || MA.f32 || M2.f32 || MA2.f32 || MA.ld % 64 || X.ld % 32 || M2.ld % 32 || MA2.ld % 32) return false;
+      // the weights as the separate launches pack them: [384][192] and [192][384], K-major
+      std::vector<float> W1((size_t)CC::N1 * CC::K1, 0.0f), W2((size_t)CC::N2 * CC::K2, 0.0f);
+      pack_conv(W1, CC::K1, CC::K1, 0, c1);
+      pack_conv(W2, CC::K2, CC::K2, 0, c2);
+      std::vector<T> w1(W1.size()), w2(W2.size());
+      for (size_t i = 0; i < W1.size(); i++) w1[i] = T(W1[i]);
+      for (size_t i = 0; i < W2.size(); i++) w2[i] = T(W2[i]);
+      std::vector<float> sc1 = next.bn->merged_scale, bi1 = next.bn->merged_bias;
+      std::vector<float> sc2 = first.bn->merged_scale, bi2 = first.bn->merged_bias;
+      sc1.resize(CC::N1, 0.0f);
+      bi1.resize(CC::N1, 0.0f);
+      sc2.resize(CC::N2, 0.0f);
+      bi2.resize(CC::N2, 0.0f);
+      ChainParams cp = {};
+      cp.rowmask = I.rowmask;
+      cp.err = I.d_err;
+      cp.scale1 = up(sc1);
+      cp.bias1 = up(bi1);
+      cp.act1 = next.act;
+      cp.scale2 = up(sc2);
+      cp.bias2 = up(bi2);
+      cp.act2 = first.act;
+      constexpr bool ebf = std::is_same<T, __nv_bfloat16>::value;
+      ChainMaps cm;
+      cm.x = make_map(MA.p, ebf, MA.ld, rows_for(MA), 128);
+      cm.w1 = make_map(up(w1), ebf, CC::K1, CC::N1, 96);
+      cm.w2 = make_map(up(w2), ebf, CC::K2, CC::N2, 96);
+      cm.trunk = make_box_map(X.p, ebf, X.ld, rows_for(X));
+      cm.raw2 = make_box_map(M2.p, ebf, M2.ld, rows_for(M2));
+      cm.act2 = make_box_map(MA2.p, ebf, MA2.ld, rows_for(MA2));
+      const int max_pairs = launch_chain<T>(true, 0, 0, cm, cp);
+      add(CLS_LINEAR, [=](cudaStream_t st, int n) {
+        ChainParams q = cp;
+        q.rows = n * 400;
+        const int tiles = (q.rows + 255) / 256;
+        launch_chain<T>(false, std::min(tiles, max_pairs), st, cm, q);
+      });
+      return true;
+    }
+  }
+
+  // Returns whether the next block's opening 1x1 was emitted with this block's closing one (pre_done for it).
+  bool emit_block(const BlockDesc& b, int depth, int C, BnAct next, bool raw_live = true, bool pre_done = false,
+                  const BlockDesc* nb = nullptr) {
     Tensor X = tensor(R_LEVEL0 + 2 * depth, C);
     Tensor XA = tensor(R_LEVEL0 + 2 * depth + 1, C);
     if (b.kind == BLOCK_ORDINARY) {
@@ -1037,14 +1140,16 @@ struct Builder {
         s.bias = first.bn->merged_bias;
         s.actout = MA;
       }
-      gemm(conv_spec(CLS_LINEAR, XA, C, {&b.pre_conv}, {s}));
+      if (!pre_done) gemm(conv_spec(CLS_LINEAR, XA, C, {&b.pre_conv}, {s}));
       emit_stack(b.inner, depth + 1, mid, {&b.post_bn, b.post_act}, false);
+      if (nb && raw_live && chain_boundary(b, *nb, depth, C, next, X, MA)) return true;
       gemm(conv_spec(CLS_LINEAR, MA, mid, {&b.post_conv}, {close_seg(w16(C), X, XA, next, false, raw_live)}));
     } else if (b.kind == BLOCK_ATTENTION) {
       emit_attention(b, X, XA, C, next);
     } else {
       emit_ffn(b, X, XA, C, next);
     }
+    return false;
   }
 
   void emit_attention(const BlockDesc& b, Tensor X, Tensor XA, int C, BnAct next) {

@@ -25,7 +25,7 @@ def forward(name, env, spatial, glob, meta=None, prec=kc.PRECISION_F16):
     """A fresh plan built under `env` (the GEMM selection is read when the plan is built)."""
     saved = {k: os.environ.get(k) for k in ("KATAGO_CUDA_PAIR", "KATAGO_CUDA_PAIR_WIN", "KATAGO_CUDA_PAIR_NARROW",
                                             "KATAGO_CUDA_PAIR_SPLIT", "KATAGO_CUDA_GPOOL_FUSED",
-                                            "KATAGO_CUDA_GPOOL_GROUPS")}
+                                            "KATAGO_CUDA_GPOOL_GROUPS", "KATAGO_CUDA_CHAIN")}
     try:
         for k in saved:
             os.environ.pop(k, None)
@@ -97,3 +97,15 @@ def test_gpool_mid_fused_is_bit_identical(prec):
         fused = forward("small-nbt", env, spatial, glob, prec=prec)
         for k in KEYS:
             np.testing.assert_array_equal(fused[k], three[k], err_msg=str(env))
+
+
+@pytest.mark.parametrize("batch", [1, 100])
+def test_chained_boundary_1x1s_match_separate_launches(batch):
+    """b18c384nbt's nested-block boundaries (closing 1x1 of one block + opening 1x1 of the next, with the trunk's
+    batch norm + mish kept in tensor memory) give the outputs of the two separate launches, bit for bit: one board,
+    and a batch whose last 256-row tile is partly filled, on mixed boards."""
+    spatial, glob, _, _ = inputs.synthetic_inputs(batch, 6100 + batch, (9, 13, 19), rich=True)
+    chained = forward("b18c384nbt", {}, spatial, glob)
+    separate = forward("b18c384nbt", {"KATAGO_CUDA_CHAIN": "0"}, spatial, glob)
+    for k in KEYS:
+        np.testing.assert_array_equal(chained[k], separate[k], err_msg=k)
