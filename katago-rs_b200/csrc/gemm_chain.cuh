@@ -14,9 +14,11 @@
 //   G2: 24 K steps (16 channels each) with A from tensor memory (channel block k at column 128 (k / 8) + 8 (k % 8))
 //       into columns [320, 512), free once E1 is done (group 2's upper half and the unused [384, 512)).
 //   E2: 64 output columns per epilogue warp group: raw and act outputs through staging boxes.
-// The next tile's G1 waits for E2 (its columns overlap the XA and G2 columns), so the phases of a pair run in
-// series; the TMA producer runs ahead through the stage ring (G1 stages: A + both weight halves; G2 stages: three
-// weight K-blocks).
+// The next tile's G1 overwrites the XA columns (dead once G2 is complete) and G2's columns [320, 384), which only
+// epilogue group 0 reads: it starts as soon as G2 is complete and group 0 has loaded its E2 columns, so it runs
+// beside the rest of E2. G2 itself reuses [384, 512) only after every warp has passed the next tile's E1, and so
+// its E2. The epilogue warps wait out one GEMM per tile (G2). The TMA producer runs ahead through the stage ring
+// (G1 stages: A + both weight halves; G2 stages: three weight K-blocks).
 // The epilogue arithmetic is the CTA-pair kernel's (residual add, raw = v * mask, pair_act), so the outputs equal the
 // two separate launches'.
 #pragma once
@@ -99,8 +101,8 @@ __global__ void __launch_bounds__(ChainCfg::THREADS, 1)
   uint64_t* t1full = empty + C::STAGES;  // G1 accumulated
   uint64_t* actready = t1full + 1;       // E1 done: XA in tensor memory, G1's columns drained
   uint64_t* t2full = actready + 1;       // G2 accumulated
-  uint64_t* tempty = t2full + 1;         // E2 has read G2's accumulator
-  uint64_t* drain = tempty + 1;
+  uint64_t* e2lo = t2full + 1;           // epilogue group 0 has read its E2 columns [320, 384)
+  uint64_t* drain = e2lo + 1;
   uint64_t* rbar = drain + 1;            // [EPI_WARPS][NRES]
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(rbar + C::NRES * C::EPI_WARPS);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
@@ -129,7 +131,7 @@ __global__ void __launch_bounds__(ChainCfg::THREADS, 1)
     mbar_init(t1full, 1);
     mbar_init(t2full, 1);
     mbar_init(actready, 2 * C::EPI_WARPS);  // one arrival per epilogue warp of both CTAs
-    mbar_init(tempty, 2 * C::EPI_WARPS);
+    mbar_init(e2lo, 2 * 4);  // group 0's four warps in both CTAs
     mbar_init(drain, 1);
     for (int i = 0; i < C::NRES * C::EPI_WARPS; i++) mbar_init(&rbar[i], 1);
     *abort_flag = 0;
@@ -224,8 +226,9 @@ __global__ void __launch_bounds__(ChainCfg::THREADS, 1)
         int lt = 0;
         for (int it = pair; it < num_tiles && ok; it += npairs, lt++) {
           const uint32_t ph = lt & 1;
-          // G1 overwrites the XA columns G2 read and G2's accumulator columns E2 read
-          if (!(ok = data_ready(tempty, ph ^ 1))) break;
+          // G1 overwrites the previous tile's XA columns (G2 complete) and its G2 columns [320, 384) (group 0's E2
+          // loads done)
+          if (!(ok = data_ready(t2full, ph ^ 1) && data_ready(e2lo, ph ^ 1))) break;
           tc_fence_after();
           for (int kb = 0; kb < C::KB1; kb++) {
             if (!(ok = data_ready(&full[stage], phase))) break;
@@ -286,7 +289,7 @@ __global__ void __launch_bounds__(ChainCfg::THREADS, 1)
     uint8_t* ring = wbuf + 2 * C::BOX;
     uint64_t* rb = rbar + C::NRES * ew;
     const uint32_t actready_l = mapa_shared(smem_u32(actready), 0);
-    const uint32_t tempty_l = mapa_shared(smem_u32(tempty), 0);
+    const uint32_t e2lo_l = mapa_shared(smem_u32(e2lo), 0);
     constexpr int E1_CHUNKS = 4, E2_CHUNKS = 2;  // 32-column chunks per warp: 128 trunk / 64 opening channels
     // residual box u (this warp's u-th E1 chunk over its tiles) into ring buffer u % NRES, NRES boxes ahead
     auto res_issue = [&](int u) {
@@ -390,10 +393,10 @@ __global__ void __launch_bounds__(ChainCfg::THREADS, 1)
         uint32_t x[32];
         tmem_ld32(tl + C::ACC2 + col, x);
         tmem_wait_ld();
-        if (cc == E2_CHUNKS - 1) {
+        if (h == 0 && cc == E2_CHUNKS - 1) {
           tc_fence_before();
           __syncwarp();
-          if (lane == 0) mbar_arrive_cluster(tempty_l);
+          if (lane == 0) mbar_arrive_cluster(e2lo_l);
         }
         float v[32];
 #pragma unroll
