@@ -193,7 +193,8 @@ int kc_get_output(kc_handle* h, int n, const float* const* spatial_rows, const f
  * class: 0 conv3x3 GEMM, 1 conv1x1/linear GEMM, 2 stem GEMM, 3 attention, 4 other kernels. */
 int kc_handle_set_profiling(kc_handle* h, int on);
 int kc_handle_profile(kc_handle* h, double* ms_by_class, int64_t* launches_by_class, int n_classes);
-/* Kernel launches per forward pass of n rows (after warm-up), and algorithmic FLOPs per row. */
+/* Kernel launches per forward pass of n positions (1 <= n <= the handle's max_batch; some boundaries of a net take
+ * one fused kernel or two kernels depending on n), and algorithmic FLOPs per row. */
 int kc_handle_launch_count(kc_handle* h, int n, int* launches);
 int kc_model_flops(const kc_model* model, double* flops_per_row, double* conv3x3_flops_per_row);
 

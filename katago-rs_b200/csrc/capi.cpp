@@ -701,8 +701,8 @@ int kc_handle_launch_count(kc_handle* h, int n, int* launches) {
   return guard([&] {
     need(h, "handle");
     need(launches, "launches");
-    (void)n;
-    *launches = h->engine->launches_per_forward();
+    if (n < 1 || n > h->max_batch) fail(KC_ERR_INVALID, "CUDA backend: launch count for a batch outside [1, max_batch]");
+    *launches = h->engine->launches_per_forward(n);
   });
 }
 

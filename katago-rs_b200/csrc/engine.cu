@@ -1036,8 +1036,12 @@ struct Builder {
   // A nested block's closing 1x1 and the next nested block's opening 1x1 as one launch (gemm_chain_kernel): the
   // trunk's batch norm + activation for the opening (XA) stays in tensor memory instead of a 384-channel HBM write
   // and read per boundary. Taken for the 2-byte tiers' 384-channel trunks with 192-channel bottlenecks (the
-  // b18c384nbt shape); KATAGO_CUDA_CHAIN=0: two launches. Returns whether it emitted the launch.
-  bool chain_boundary(const BlockDesc& b, const BlockDesc& nb, int depth, int C, BnAct next, Tensor X, Tensor MA) {
+  // b18c384nbt shape) when a batch has at least half as many 256-row tiles as SM pairs: below that the two separate
+  // launches, whose narrow tiles spread over more pairs, are faster (batch 1: 804 against 764 evals/s, batch 8:
+  // 5,928 against 5,821; batch 32: 18,090 against 18,926), so both are built and each forward picks one.
+  // KATAGO_CUDA_CHAIN=0: always the two launches. Returns whether it emitted the boundary.
+  bool chain_boundary(const BlockDesc& b, const BlockDesc& nb, int depth, int C, BnAct next, Tensor X, Tensor XA,
+                      Tensor MA) {
     if constexpr (sizeof(T) != 2) {
       return false;
     } else {
@@ -1084,12 +1088,34 @@ struct Builder {
       cm.raw2 = make_box_map(M2.p, ebf, M2.ld, rows_for(M2));
       cm.act2 = make_box_map(MA2.p, ebf, MA2.ld, rows_for(MA2));
       const int max_pairs = launch_chain<T>(true, 0, 0, cm, cp);
+      // the two separate launches (as emit_block would record them), taken out of the plan for small batches
+      const size_t mark = plan.size();
+      gemm(conv_spec(CLS_LINEAR, MA, c1.ic, {&c1}, {close_seg(w16(C), X, XA, next, false)}));
+      Seg so;
+      so.width = w16(c2.oc);
+      so.flags = EPI_RAW | EPI_ACT;
+      so.raw = M2;
+      so.act = first.act;
+      so.scale = first.bn->merged_scale;
+      so.bias = first.bn->merged_bias;
+      so.actout = MA2;
+      gemm(conv_spec(CLS_LINEAR, XA, C, {&c2}, {so}));
+      std::vector<std::function<void(cudaStream_t, int)>> sep;
+      for (size_t i = mark; i < plan.size(); i++) sep.push_back(plan[i].fn);
+      plan.resize(mark);
+      auto chained = [max_pairs](int n) { return 2 * ((n * 400 + 255) / 256) >= max_pairs; };
       add(CLS_LINEAR, [=](cudaStream_t st, int n) {
         ChainParams q = cp;
         q.rows = n * 400;
         const int tiles = (q.rows + 255) / 256;
-        launch_chain<T>(false, std::min(tiles, max_pairs), st, cm, q);
+        if (chained(n)) {
+          launch_chain<T>(false, std::min(tiles, max_pairs), st, cm, q);
+        } else {
+          for (const auto& f : sep) f(st, n);
+        }
       });
+      const int n_sep = (int)sep.size();
+      plan.back().kernels = [chained, n_sep](int n) { return chained(n) ? 1 : n_sep; };
       return true;
     }
   }
@@ -1142,7 +1168,7 @@ struct Builder {
       }
       if (!pre_done) gemm(conv_spec(CLS_LINEAR, XA, C, {&b.pre_conv}, {s}));
       emit_stack(b.inner, depth + 1, mid, {&b.post_bn, b.post_act}, false);
-      if (nb && raw_live && chain_boundary(b, *nb, depth, C, next, X, MA)) return true;
+      if (nb && raw_live && chain_boundary(b, *nb, depth, C, next, X, XA, MA)) return true;
       gemm(conv_spec(CLS_LINEAR, MA, mid, {&b.post_conv}, {close_seg(w16(C), X, XA, next, false, raw_live)}));
     } else if (b.kind == BLOCK_ATTENTION) {
       emit_attention(b, X, XA, C, next);

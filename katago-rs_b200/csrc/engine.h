@@ -41,7 +41,12 @@ class Engine {
   int max_batch() const { return max_batch_; }
   int precision() const { return precision_; }
   int device() const { return device_; }
-  int launches_per_forward() const { return (int)plan_.size(); }
+  // Kernel launches of a forward pass of n boards (an entry of the plan may choose between forms by batch).
+  int launches_per_forward(int n) const {
+    int k = 0;
+    for (const Launch& l : plan_) k += l.kernels ? l.kernels(n) : 1;
+    return k;
+  }
   // Non-zero after a kernel reported a device-side error (a bounded wait expired).
   int device_error();
   int* error_word();  // device address of the error word kernels write (first error wins)
@@ -57,6 +62,7 @@ class Engine {
   struct Launch {
     int cls;
     std::function<void(cudaStream_t, int)> fn;
+    std::function<int(int)> kernels;  // kernels fn launches for n boards (empty: one)
   };
 
  private:

@@ -99,13 +99,22 @@ def test_gpool_mid_fused_is_bit_identical(prec):
             np.testing.assert_array_equal(fused[k], three[k], err_msg=str(env))
 
 
-@pytest.mark.parametrize("batch", [1, 100])
+@pytest.mark.parametrize("batch", [1, 37, 100])
 def test_chained_boundary_1x1s_match_separate_launches(batch):
     """b18c384nbt's nested-block boundaries (closing 1x1 of one block + opening 1x1 of the next, with the trunk's
-    batch norm + mish kept in tensor memory) give the outputs of the two separate launches, bit for bit: one board,
-    and a batch whose last 256-row tile is partly filled, on mixed boards."""
+    batch norm + mish kept in tensor memory) give the outputs of the two separate launches, bit for bit, on mixed
+    boards: 37 and 100 boards (58 and 157 row tiles, the last partly filled) run the chained kernel; one board (two
+    row tiles) runs the separate launches that small batches take."""
     spatial, glob, _, _ = inputs.synthetic_inputs(batch, 6100 + batch, (9, 13, 19), rich=True)
     chained = forward("b18c384nbt", {}, spatial, glob)
     separate = forward("b18c384nbt", {"KATAGO_CUDA_CHAIN": "0"}, spatial, glob)
     for k in KEYS:
         np.testing.assert_array_equal(chained[k], separate[k], err_msg=k)
+
+
+def test_launch_count_follows_the_boundary_form():
+    """The handle's launch count is per batch: b18c384nbt's 17 nested-block boundaries take two launches each at one
+    board and one chained launch at 64 boards (at least half as many 256-row tiles as the B200's 74 SM pairs)."""
+    m = kc.Model(netgen.net_bytes("b18c384nbt"))
+    h = kc.Handle(kc.Context(m, gpu_idxs=[0], precision=kc.PRECISION_F16), max_batch=64, gpu_idx=0)
+    assert h.launch_count(1) - h.launch_count(64) == 17
