@@ -62,6 +62,9 @@ struct ChainCfg {
   static constexpr uint32_t TMEM_COLS = 512;
   static constexpr uint32_t ACC2 = 320;  // G2's accumulator: columns [320, 512)
   static_assert(ACC2 + N2 <= TMEM_COLS && ACC2 >= 2 * 128 + 64, "G2 columns free after E1");
+  // the next tile's G1 may start once epilogue group 0 has read its E2 columns [ACC2, ACC2 + 64): G1's columns
+  // [0, N1) must meet G2's only there
+  static_assert(N1 - ACC2 <= N2 / 3, "G1 / G2 column overlap inside group 0's E2 columns");
   // registers: as the 12-warp pair tiles (warpgroup 0: producer, MMA issuer, two idle warps)
   static constexpr int WG0_REGS = 48, EPI_REGS = 152;
   static_assert(4 * 32 * WG0_REGS + 12 * 32 * EPI_REGS <= 65536, "register split");
